@@ -1,0 +1,157 @@
+/*
+ * fp8mla.h -- C ABI of the B200 (sm_100a) fp8_ds_mla sparse-MLA decode library
+ * (libfp8mla.so).
+ *
+ * Every entry point takes plain device pointers, 64-bit sizes and element
+ * strides, and a CUDA stream passed as `void*` (a cudaStream_t; NULL = the
+ * legacy default stream).  No torch or CUDA types appear in the signatures.
+ * Every call returns an int status (FP8MLA_OK = 0, negative on error); the
+ * message of the last failure on the calling thread is available from
+ * fp8mla_last_error().  Calls are asynchronous with respect to the host
+ * unless stated otherwise, and none of them synchronises the stream.
+ *
+ * fp8_ds_mla row (656 bytes per KV slot), the format this library reads and
+ * writes (reference: vllm_fp8kv/fp8_ds_mla_sparse_decode.py:41-47, :68-74):
+ *     [  0:512)  512 x float8_e4m3fn   NoPE latent, per-128-tile scaled
+ *     [512:528)    4 x float32         per-128-element tile scales (amax/448)
+ *     [528:656)   64 x bfloat16        RoPE, stored raw (never quantized)
+ */
+#ifndef FP8MLA_H
+#define FP8MLA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define FP8MLA_OK 0
+#define FP8MLA_ERR_INVALID_ARGUMENT (-1) /* shape, dtype, stride or alignment */
+#define FP8MLA_ERR_UNSUPPORTED (-2)      /* device is not sm_100 / no kernel  */
+#define FP8MLA_ERR_CUDA (-3)             /* a CUDA runtime call failed        */
+#define FP8MLA_ERR_WORKSPACE (-4)        /* workspace missing or too small    */
+
+/* ---- element types ------------------------------------------------------- */
+#define FP8MLA_DTYPE_BF16 0
+#define FP8MLA_DTYPE_F32 1
+#define FP8MLA_DTYPE_F16 2
+
+/* ---- row geometry (reference: fp8_ds_mla_sparse_decode.py:68-74) --------- */
+#define FP8MLA_NOPE 512
+#define FP8MLA_ROPE 64
+#define FP8MLA_TILE 128
+#define FP8MLA_ROW_BYTES 656
+#define FP8MLA_SCALE_OFF 512
+#define FP8MLA_ROPE_OFF 528
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* fp8mla_last_error(void);
+
+/* ABI version of this library (bumped on any signature change). */
+int fp8mla_abi_version(void);
+
+/*
+ * Split-KV count the decode picks when called with num_splits = 0.
+ * Replaces the host heuristic `_choose_num_kv_splits`
+ * (tests/fixtures/triton_mla_sparse_kernel_pr47629.py:406-423): a power of two
+ * in {1,2,4,8,16}, 1 when T * head_blocks * 4 >= sm_count, at least 128 top-k
+ * entries per split, and topk divisible by the count.
+ */
+int fp8mla_choose_num_splits(int64_t T, int64_t H, int64_t G, int64_t topk,
+                             int sm_count);
+
+/*
+ * Bytes of device workspace fp8mla_sparse_decode needs for this shape and
+ * split count (0 when num_splits == 1).  Pass num_splits = 0 to size for the
+ * count fp8mla_choose_num_splits() returns on the current device.
+ */
+int64_t fp8mla_decode_workspace_bytes(int64_t T, int64_t H, int64_t G,
+                                      int64_t topk, int num_splits);
+
+/*
+ * Sparse MLA decode over fp8_ds_mla pages.
+ *
+ * Replaces the Triton launch behind `fp8_ds_mla_sparse_decode`
+ * (vllm_fp8kv/fp8_ds_mla_sparse_decode.py:214-288, kernel :77-211) and the
+ * upstream split-KV pair `_sparse_mla_kernel_split` + `_sparse_mla_merge_kernel`
+ * (tests/fixtures/triton_mla_sparse_kernel_pr47629.py:232-403).
+ *
+ *   q        [T, H, 576]   bf16 (q_dtype = FP8MLA_DTYPE_BF16) or fp32
+ *                          (FP8MLA_DTYPE_F32, rounded to bf16 on load);
+ *                          unit stride on the last dim.
+ *   kv       [num_slots, 656] uint8, contiguous, 16-byte aligned.
+ *   indices  [T, G, topk]  int32 flat slot indices; entries < 0 or
+ *                          >= num_slots are masked (no load is issued).
+ *                          Head h reads group h / (H / G).
+ *   sm_scale softmax scale WITHOUT the log2(e) factor.
+ *   out      [T, H, 512]   same dtype as q.
+ *   lse      [T, H] fp32 natural-log LSE, or NULL.  -inf for a row that
+ *                          selected nothing (its out row is all zeros).
+ *   num_splits  0 = fp8mla_choose_num_splits(); otherwise 1..64 splits of the
+ *               top-k axis merged by LSE.  Splits > 1 need `workspace`.
+ *
+ * Returns FP8MLA_ERR_INVALID_ARGUMENT for shape/stride/alignment violations.
+ */
+int fp8mla_sparse_decode(const void* q, int q_dtype, int64_t T, int64_t H,
+                         int64_t q_stride_t, int64_t q_stride_h,
+                         const uint8_t* kv, int64_t num_slots,
+                         const int32_t* indices, int64_t G, int64_t topk,
+                         int64_t idx_stride_t, int64_t idx_stride_g,
+                         float sm_scale,
+                         void* out, int64_t out_stride_t, int64_t out_stride_h,
+                         float* lse, int64_t lse_stride_t,
+                         int num_splits, void* workspace,
+                         int64_t workspace_bytes, void* stream);
+
+/*
+ * fp8_ds_mla cache writer: quantize bf16 latent + rope into 656-byte rows.
+ *
+ * Replaces vLLM's `concat_and_cache_mla(..., kv_cache_dtype="fp8_ds_mla")`
+ * (called at verify/contract.py:100-103), whose behaviour the reference
+ * restates in verify/reference.py:68-91 and tests/fakes.py:28-57: per
+ * 128-element tile, scale = max(amax / 448, FLT_MIN); latent byte =
+ * float8_e4m3fn(x / scale) with round-to-nearest-even (|v| >= 464 rounds to
+ * the NaN encoding 0x7F, as torch's cast does); rope copied as raw bf16.
+ * The layer's k_scale is not an input: the format ignores it.
+ *
+ *   kv_c  [N, 512] bf16 bits, row stride kv_c_stride (elements)
+ *   k_pe  [N, 64]  bf16 bits, row stride k_pe_stride (elements)
+ *   slot_mapping [N] int64; slots < 0 or >= num_slots are skipped.
+ *   cache [num_slots, 656] uint8
+ */
+int fp8mla_ds_mla_write(const uint16_t* kv_c, int64_t kv_c_stride,
+                        const uint16_t* k_pe, int64_t k_pe_stride,
+                        const int64_t* slot_mapping, int64_t N,
+                        uint8_t* cache, int64_t num_slots, void* stream);
+
+/*
+ * Device e4m3fn decode of n raw bytes into fp16 / bf16 / fp32 (out_dtype).
+ * method 0 = the packed hardware conversion, 1 = the integer bit-math the
+ * fused decode uses.  Both are exact for every finite byte; 0x7F/0xFF give NaN.
+ * Replaces `_dequant_test_kernel` / `dequant_triton_launch`
+ * (vllm_fp8kv/fp8_dequant.py:98-113).
+ */
+int fp8mla_dequant_e4m3(const uint8_t* in, int64_t n, void* out,
+                        int out_dtype, int method, void* stream);
+
+/*
+ * Token-relative top-k -> flat global slot:
+ *   out[t, i] = block_table[req_id[t], tok / block_size] * block_size
+ *               + tok % block_size,  with tok = token_idx[t, i];
+ * -1 when tok < 0 or the block index is outside [0, max_blocks).
+ * Replaces vLLM's `triton_convert_req_index_to_global_index`
+ * (called at vllm_fp8kv/backend_patch.py:83-89; mirrored in
+ * tests/fakes.py:70-82).  topk must be a multiple of 128.
+ */
+int fp8mla_convert_req_index(const int32_t* req_id, const int32_t* block_table,
+                             int64_t bt_stride, int64_t max_blocks,
+                             const int32_t* token_idx, int64_t ti_stride,
+                             int64_t T, int64_t topk, int64_t block_size,
+                             int32_t* out, int64_t out_stride, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FP8MLA_H */
