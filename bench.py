@@ -1,0 +1,398 @@
+"""Benchmark: fp8 sparse-MLA decode on B200, B=64, H=128, top-k=2048 per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c2|c3|c4|c5]
+
+One step = one decode call over one batch (64 requests x 128 heads x 2048
+selected 656-byte rows).  Multi-GPU: one process per GPU (torchrun), requests
+and their KV pages sharded across GPUs (weak scaling, per-GPU batch fixed), no
+collective on the hot path; the timed window is bracketed by barriers and the
+step time is the max over ranks.  Rank 0 prints one JSON line.
+
+value      = KV GB/s of the whole job = (N * B * topk * 656 bytes) / step time
+e2e        = same metric through the public Python API with the step's q and
+             indices copied from pinned host memory and out copied back
+roofline   = the decode kernel's achieved TFLOP/s (or GB/s for the HBM-bound
+             shapes) from CUDA events on its stream, against MEASURED_PEAKS.json
+cpu_baseline = the oracle's numpy restatement of the reference's fp32 torch
+             golden path, on a bounded sample of the same workload, rank 0, N=1
+--impl reference = that CPU implementation alone, as the reference arm
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "vllm-fp8kv_b200"))
+sys.path.insert(0, REPO)
+
+import numpy as np  # noqa: E402
+
+METRIC = "fp8 sparse-MLA decode µs/call + KV GB/s, B=64,H=128,topk=2048, 1/2/4/8 GPU"
+N_SETS = 4  # rotating (q, indices) sets: consecutive steps read disjoint KV rows
+
+
+def _env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Polls NVML (SM clock, throttle reasons) in a thread during the timed region."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.samples, self.reasons = [], 0
+        self.period = period_s
+        self._stop = threading.Event()
+        self._ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._ok = True
+        except Exception as e:  # NVML missing: report it instead of guessing
+            self.err = repr(e)
+            self.max_mhz = None
+
+    def _run(self):
+        nv, h = self._nv, self._h
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                self.reasons |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self._ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self._ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": self.err}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit]
+        med = float(np.median(self.samples)) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+def _peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def _traffic_per_launch(kernel: str, workload: str):
+    """dram read+write bytes per launch from the committed ncu summary, if any."""
+    path = os.path.join(REPO, "profiles", f"{kernel}_{workload}.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(float(line.split(":", 1)[1].strip()))
+            except ValueError:
+                return None
+    return None
+
+
+# ---------------------------------------------------------------- CPU arm
+def cpu_reference_step_fn(shape_name: str, sample_requests: int, seed: int = 0):
+    """Build a bounded CPU sample of the workload and return (fn, kv_bytes, desc).
+
+    The sample keeps the per-request shape (heads, top-k, context length, page
+    size, value distributions) and builds only `sample_requests` requests
+    with their own KV pages, quantized by the oracle writer on the host."""
+    from oracle import oracle as O
+    from vllm_fp8kv import synthetic
+
+    s = synthetic.SHAPES[shape_name]
+    B = min(sample_requests, s.B)
+    pool_slots = B * s.ctx if not s.shared_pool else max(B * 2048 * 64, 1 << 20)
+    w = synthetic.make_host(s, seed=seed, B=B, pool_slots=min(pool_slots, s.pool_slots))
+    pool = O.quantize_rows(w.kv_src_bits)
+    q = synthetic.bf16_to_f32(w.q_bits)
+    slots = w.slots
+
+    def fn():
+        return O.sparse_decode(q, pool, slots, w.sm_scale)
+
+    desc = (f"{B} of {s.B} requests of {shape_name} (H={s.H}, topk={s.topk}, ctx={s.ctx}); "
+            f"numpy fp32 restatement of ref_sparse_mla_decode + logsumexp, BLAS threads")
+    return fn, B * s.topk * 656, desc
+
+
+def run_reference_arm(args, rank):
+    if rank != 0:
+        return None
+    try:
+        import threadpoolctl
+
+        threadpoolctl.threadpool_limits(os.cpu_count())
+    except Exception:
+        pass
+    fn, kv_bytes, desc = cpu_reference_step_fn(args.workload, args.cpu_sample)
+    for _ in range(args.warmup):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fn()
+    dt = (time.perf_counter() - t0) / args.steps
+    gbs = kv_bytes / dt / 1e9
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "sample": desc},
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    return line
+
+
+# ---------------------------------------------------------------- GPU arm
+def run_ours(args, rank, world, local_rank):
+    import torch
+
+    from vllm_fp8kv import synthetic
+    from vllm_fp8kv.fp8_ds_mla_sparse_decode import (
+        decode_workspace_bytes,
+        fp8_ds_mla_sparse_decode,
+    )
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    s = synthetic.SHAPES[args.workload]
+    w = synthetic.make_device(s, seed=1000 + rank, device=dev)
+    splits = s.num_splits or None
+    # rotating input sets over the same pool: fresh top-k rows every step
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    sets = [(w.q, w.slots)]
+    for _ in range(N_SETS - 1):
+        tok = torch.rand((s.B, s.ctx), generator=g, device=dev).argsort(dim=1)[:, : s.topk]
+        tok = tok.to(torch.int32)
+        if s.lead_masked_reqs:
+            tok[: s.lead_masked_reqs, : s.lead_masked] = -1
+        valid = tok >= 0
+        t0 = torch.where(valid, tok, torch.zeros_like(tok)).long()
+        page = torch.gather(w.block_table.long(), 1, t0 // 64)
+        slots = torch.where(valid, page * 64 + t0 % 64, torch.full_like(page, -1)).to(torch.int32)
+        q = torch.randn((s.B, s.H, 576), generator=g, device=dev).to(torch.bfloat16)
+        sets.append((q, slots.contiguous()))
+    ws_bytes = decode_workspace_bytes(s.B, s.H, 1, s.topk, splits or 0)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    kv = w.kv
+
+    def step(i):
+        q, sl = sets[i % N_SETS]
+        return fp8_ds_mla_sparse_decode(q, kv, sl, w.sm_scale, return_lse=True,
+                                        num_kv_splits=splits, workspace=ws)
+
+    stream = torch.cuda.current_stream(dev)
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+
+    # ---- device-timed window: K steps, per-launch events on the launching stream
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        w0.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            step(i)
+            ends[i].record(stream)
+        w1.record(stream)
+        torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    window_ms = w0.elapsed_time(w1)
+    launch_ms = float(np.mean([a.elapsed_time(b) for a, b in zip(starts, ends)]))
+    step_ms = window_ms / args.steps
+
+    # ---- end to end through the public API: pinned host q/indices in, out back
+    hq = [sq.cpu().pin_memory() for sq, _ in sets]
+    hi = [sl.cpu().pin_memory() for _, sl in sets]
+    hout = torch.empty((s.B, s.H, 512), dtype=torch.bfloat16).pin_memory()
+    hlse = torch.empty((s.B, s.H), dtype=torch.float32).pin_memory()
+    dq = [torch.empty_like(sq) for sq, _ in sets]
+    di = [torch.empty_like(sl) for _, sl in sets]
+
+    def e2e_step(i):
+        k = i % N_SETS
+        dq[k].copy_(hq[k], non_blocking=True)
+        di[k].copy_(hi[k], non_blocking=True)
+        out, lse = fp8_ds_mla_sparse_decode(dq[k], kv, di[k], w.sm_scale, return_lse=True,
+                                            num_kv_splits=splits, workspace=ws)
+        hout.copy_(out, non_blocking=True)
+        hlse.copy_(lse, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    h2d = sets[0][0].numel() * 2 + sets[0][1].numel() * 4
+    d2h = hout.numel() * 2 + hlse.numel() * 4
+
+    # ---- max over ranks (no collective on the hot path; this is after timing)
+    vals = torch.tensor([step_ms, e2e_ms, launch_ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    step_ms, e2e_ms, launch_ms = vals.tolist()
+
+    from vllm_fp8kv.fp8_ds_mla_sparse_decode import decode_kernel_name
+
+    kerns = decode_kernel_name(s.B, s.H, 1, s.topk, torch.bfloat16, splits or 0)
+    kern = kerns.split("+")[0]
+    launches_per_step = len(kerns.split("+"))
+    line = None
+    if rank == 0:
+        kvb = synthetic.kv_bytes(s.B, s.topk)
+        flops = synthetic.algorithmic_flops(s.B, s.H, s.topk)
+        alg = synthetic.algorithmic_bytes(s.B, s.H, s.topk)
+        peaks = _peaks()
+        tensor_bound = s.H >= 64
+        if tensor_bound:
+            achieved = flops / (launch_ms * 1e-3) / 1e12
+            peak = peaks["bf16_tflops"]
+            roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak}
+        else:
+            achieved = alg / (launch_ms * 1e-3) / 1e9
+            peak = peaks["hbm_gbs"]
+            roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": achieved / peak}
+        roof["peak_source"] = peaks["source"] + " (burst)"
+        roof["kernel"] = kern
+        roof["launch_us"] = launch_ms * 1e3
+        roof["traffic"] = _traffic_per_launch(kern, args.workload)
+        roof["algorithmic_bytes_per_launch"] = alg
+        roof["algorithmic_flops_per_launch"] = flops
+        value = world * kvb / (step_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "us_per_call": step_ms * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {
+                "workload": f"{args.workload}: B={s.B} H={s.H} topk={s.topk} ctx={s.ctx} "
+                            f"pool={s.pool_slots} slots page=64 per GPU",
+                "per_gpu_batch": s.B, "global_batch": s.B * world, "heads": s.H,
+                "topk": s.topk, "num_kv_splits": splits or "auto",
+                "parallelism": f"request-sharded x{world}, no collective",
+                "l2": f"{N_SETS} rotating q/top-k sets over a {s.pool_slots * 656 / 1e9:.2f} GB "
+                      f"pool: {N_SETS * kvb / 1e6:.0f} MB of distinct rows per cycle > 126 MB L2",
+            },
+            "tflops": world * flops / (step_ms * 1e-3) / 1e12,
+            "roofline": roof,
+            "e2e": {"value": world * kvb / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                    "us_per_call": e2e_ms * 1e3, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * launches_per_step,
+            "clocks": clk.summary(),
+        }
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5"])
+    ap.add_argument("--cpu-sample", type=int, default=8,
+                    help="requests in the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = _env_int("RANK", 0)
+    world = _env_int("WORLD_SIZE", 1)
+    local_rank = _env_int("LOCAL_RANK", 0)
+
+    if args.impl == "reference":
+        line = run_reference_arm(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    line = run_ours(args, rank, world, local_rank)
+    if rank == 0 and line is not None:
+        if world == 1 and not args.no_cpu_baseline:
+            fn, kv_bytes, desc = cpu_reference_step_fn(args.workload, args.cpu_sample)
+            fn()
+            t0 = time.perf_counter()
+            n = 0
+            while True:
+                fn()
+                n += 1
+                if time.perf_counter() - t0 > 5.0 or n >= 20:
+                    break
+            dt = (time.perf_counter() - t0) / n
+            line["cpu_baseline"] = {"value": kv_bytes / dt / 1e9, "unit": "GB/s",
+                                    "cores": os.cpu_count(), "kind": "port",
+                                    "sample": desc + f"; {n} timed calls"}
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -21,6 +21,12 @@
 
 #include <stdint.h>
 
+#if defined(__GNUC__)
+#define FP8MLA_API __attribute__((visibility("default")))
+#else
+#define FP8MLA_API
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -46,10 +52,10 @@ extern "C" {
 #define FP8MLA_ROPE_OFF 528
 
 /* Message of the last failed call on this thread ("" if none). */
-const char* fp8mla_last_error(void);
+FP8MLA_API const char* fp8mla_last_error(void);
 
 /* ABI version of this library (bumped on any signature change). */
-int fp8mla_abi_version(void);
+FP8MLA_API int fp8mla_abi_version(void);
 
 /*
  * Split-KV count the decode picks when called with num_splits = 0.
@@ -58,7 +64,7 @@ int fp8mla_abi_version(void);
  * in {1,2,4,8,16}, 1 when T * head_blocks * 4 >= sm_count, at least 128 top-k
  * entries per split, and topk divisible by the count.
  */
-int fp8mla_choose_num_splits(int64_t T, int64_t H, int64_t G, int64_t topk,
+FP8MLA_API int fp8mla_choose_num_splits(int64_t T, int64_t H, int64_t G, int64_t topk,
                              int sm_count);
 
 /*
@@ -66,8 +72,19 @@ int fp8mla_choose_num_splits(int64_t T, int64_t H, int64_t G, int64_t topk,
  * split count (0 when num_splits == 1).  Pass num_splits = 0 to size for the
  * count fp8mla_choose_num_splits() returns on the current device.
  */
-int64_t fp8mla_decode_workspace_bytes(int64_t T, int64_t H, int64_t G,
+FP8MLA_API int64_t fp8mla_decode_workspace_bytes(int64_t T, int64_t H, int64_t G,
                                       int64_t topk, int num_splits);
+
+/*
+ * Name of the decode kernel fp8mla_sparse_decode dispatches for this shape
+ * ("decode_tc_kernel" for 128 heads per kv group with bf16 q, else
+ * "decode_mma_kernel"; "+merge_splits_kernel" is appended when the call splits
+ * the top-k axis).  Host-only; introspection for benchmarks and profiling.
+ * No reference counterpart (the reference has one Triton kernel per path).
+ */
+FP8MLA_API const char* fp8mla_decode_kernel_name(int64_t T, int64_t H, int64_t G,
+                                                 int64_t topk, int q_dtype,
+                                                 int num_splits);
 
 /*
  * Sparse MLA decode over fp8_ds_mla pages.
@@ -93,7 +110,7 @@ int64_t fp8mla_decode_workspace_bytes(int64_t T, int64_t H, int64_t G,
  *
  * Returns FP8MLA_ERR_INVALID_ARGUMENT for shape/stride/alignment violations.
  */
-int fp8mla_sparse_decode(const void* q, int q_dtype, int64_t T, int64_t H,
+FP8MLA_API int fp8mla_sparse_decode(const void* q, int q_dtype, int64_t T, int64_t H,
                          int64_t q_stride_t, int64_t q_stride_h,
                          const uint8_t* kv, int64_t num_slots,
                          const int32_t* indices, int64_t G, int64_t topk,
@@ -120,7 +137,7 @@ int fp8mla_sparse_decode(const void* q, int q_dtype, int64_t T, int64_t H,
  *   slot_mapping [N] int64; slots < 0 or >= num_slots are skipped.
  *   cache [num_slots, 656] uint8
  */
-int fp8mla_ds_mla_write(const uint16_t* kv_c, int64_t kv_c_stride,
+FP8MLA_API int fp8mla_ds_mla_write(const uint16_t* kv_c, int64_t kv_c_stride,
                         const uint16_t* k_pe, int64_t k_pe_stride,
                         const int64_t* slot_mapping, int64_t N,
                         uint8_t* cache, int64_t num_slots, void* stream);
@@ -132,7 +149,7 @@ int fp8mla_ds_mla_write(const uint16_t* kv_c, int64_t kv_c_stride,
  * Replaces `_dequant_test_kernel` / `dequant_triton_launch`
  * (vllm_fp8kv/fp8_dequant.py:98-113).
  */
-int fp8mla_dequant_e4m3(const uint8_t* in, int64_t n, void* out,
+FP8MLA_API int fp8mla_dequant_e4m3(const uint8_t* in, int64_t n, void* out,
                         int out_dtype, int method, void* stream);
 
 /*
@@ -144,7 +161,7 @@ int fp8mla_dequant_e4m3(const uint8_t* in, int64_t n, void* out,
  * (called at vllm_fp8kv/backend_patch.py:83-89; mirrored in
  * tests/fakes.py:70-82).  topk must be a multiple of 128.
  */
-int fp8mla_convert_req_index(const int32_t* req_id, const int32_t* block_table,
+FP8MLA_API int fp8mla_convert_req_index(const int32_t* req_id, const int32_t* block_table,
                              int64_t bt_stride, int64_t max_blocks,
                              const int32_t* token_idx, int64_t ti_stride,
                              int64_t T, int64_t topk, int64_t block_size,

@@ -105,12 +105,18 @@ float oracle_bf16_to_f32(uint16_t h) { return bits_f32((uint32_t)h << 16); }
  * element is e4m3 * scale multiplied in fp32; the rope is bf16 widened.
  */
 void oracle_dequant_rows(const uint8_t* rows, int64_t n, float* out) {
+  static float lut[256];
+  static int lut_ready = 0;
+  if (!lut_ready) { /* 256-entry table of oracle_e4m3_to_f32 (benign race: same values) */
+    for (int b = 0; b < 256; ++b) lut[b] = oracle_e4m3_to_f32((uint8_t)b);
+    lut_ready = 1;
+  }
   for (int64_t i = 0; i < n; ++i) {
     const uint8_t* r = rows + i * ROW_BYTES;
     float* o = out + i * (NOPE + ROPE);
     float sc[N_TILES];
     memcpy(sc, r + SCALE_OFF, sizeof(sc));
-    for (int d = 0; d < NOPE; ++d) o[d] = oracle_e4m3_to_f32(r[d]) * sc[d / TILE];
+    for (int d = 0; d < NOPE; ++d) o[d] = lut[r[d]] * sc[d / TILE];
     for (int d = 0; d < ROPE; ++d) {
       uint16_t h;
       memcpy(&h, r + ROPE_OFF + 2 * d, 2);

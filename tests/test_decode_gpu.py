@@ -1,0 +1,267 @@
+"""GPU parity of the sm_100a decode against the oracle and the reference's golden vectors.
+
+Mirrors the reference's decode tests (tests/test_sparse_decode.py:44-194) and
+harness sections (verify/run_all.py:78-185), with the north-star tolerance:
+max-abs <= 2e-2 and cosine >= 0.9999 against the fp32 golden path.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests import gpu_util as U
+from tests.conftest import golden
+from vllm_fp8kv import synthetic
+from vllm_fp8kv.fp8_ds_mla_sparse_decode import NOPE, ROW_BYTES, fp8_ds_mla_sparse_decode
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(q, pool, idx, sm, **kw):
+    out, lse = fp8_ds_mla_sparse_decode(q, pool, idx, sm, return_lse=True, **kw)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy(), lse.cpu().numpy()
+
+
+# ------------------------------------------------------------ golden fixtures
+@pytest.mark.parametrize("splits", [None, 1, 2, 4])
+def test_c1_matches_reference_golden(cuda_device, splits):
+    g = golden("decode_c1.npz")
+    w = synthetic.make_host("c1", seed=0)
+    pool = U.device_pool(w.kv_src_bits)
+    q = U.bf16_tensor(w.q_bits)
+    idx = torch.from_numpy(w.slots).cuda()
+    out, lse = _run(q, pool, idx, float(g["sm_scale"]), num_kv_splits=splits)
+    U.assert_close(out, g["ref_out"])
+    U.assert_lse_close(lse, g["ref_lse"])
+    # tighter: the oracle with the tensor-core operand rounding
+    ko, _ = O.sparse_decode(synthetic.bf16_to_f32(w.q_bits), pool.view(-1, 656).cpu().numpy(),
+                            w.slots, float(g["sm_scale"]), kernel_rounding=True)
+    U.assert_close(out, ko, max_abs=U.MAX_ABS_KERNEL_ROUNDING)
+
+
+TRAPS = ["masked", "leading_one", "leading_48", "empty_row", "out_of_range",
+         "groups2_h32", "heads8", "matrix_q4"]
+
+
+@pytest.mark.parametrize("case", TRAPS)
+@pytest.mark.parametrize("qdtype", [torch.float32, torch.bfloat16])
+def test_trap_cases_match_reference(cuda_device, case, qdtype):
+    g = golden("traps.npz")
+    q = torch.from_numpy(g[f"{case}__q"]).cuda().to(qdtype)
+    pool = torch.from_numpy(g[str(g[f"{case}__pool"])]).cuda()
+    idx = torch.from_numpy(g[f"{case}__idx"]).cuda()
+    out, lse = _run(q, pool, idx, float(g["sm_scale"]))
+    assert out.dtype == np.float32
+    ref_q = q.float().cpu().numpy()
+    ref, ref_lse = O.sparse_decode(ref_q, g[str(g[f"{case}__pool"])], g[f"{case}__idx"],
+                                   float(g["sm_scale"]))
+    U.assert_close(out, ref)
+    U.assert_lse_close(lse, ref_lse)
+    if qdtype == torch.float32:   # same inputs as the reference's own kernel run
+        U.assert_close(out, g[f"{case}__ref_out"])
+
+
+def test_empty_row_is_zero_with_minus_inf_lse(cuda_device):
+    g = golden("traps.npz")
+    q = torch.from_numpy(g["empty_row__q"]).cuda().bfloat16()
+    pool = torch.from_numpy(g[str(g["empty_row__pool"])]).cuda()
+    idx = torch.from_numpy(g["empty_row__idx"]).cuda()
+    for splits in (1, 2, 8):
+        out, lse = _run(q, pool, idx, float(g["sm_scale"]), num_kv_splits=splits)
+        assert not out[1].any() and np.isneginf(lse[1]).all()
+        assert out[0].any() and np.isfinite(lse[0]).all()
+
+
+def test_leading_fully_masked_splits_do_not_poison(cuda_device):
+    """Fully masked leading chunks AND whole leading splits (north-star item 4)."""
+    w = synthetic.make_host("c1", seed=3)
+    pool = U.device_pool(w.kv_src_bits)
+    slots = w.slots.copy()
+    slots[:, :192] = -1                       # 3 of 4 splits of 64 fully masked
+    q = U.bf16_tensor(w.q_bits)
+    ref, ref_lse = O.sparse_decode(synthetic.bf16_to_f32(w.q_bits), pool.view(-1, 656).cpu().numpy(),
+                                   slots, w.sm_scale)
+    for splits in (1, 2, 4, 8):
+        out, lse = _run(q, pool, torch.from_numpy(slots).cuda(), w.sm_scale, num_kv_splits=splits)
+        U.assert_close(out, ref)
+        U.assert_lse_close(lse, ref_lse)
+
+
+def test_2d_and_3d_indices_and_fp8_view_and_paged_shape_agree(cuda_device):
+    w = synthetic.make_host("c1", seed=4)
+    pool = U.device_pool(w.kv_src_bits)
+    q = U.bf16_tensor(w.q_bits)
+    idx = torch.from_numpy(w.slots).cuda()
+    a = fp8_ds_mla_sparse_decode(q, pool, idx, w.sm_scale)
+    b = fp8_ds_mla_sparse_decode(q, pool.view(-1, ROW_BYTES), idx.unsqueeze(1), w.sm_scale)
+    c = fp8_ds_mla_sparse_decode(q, pool.view(torch.float8_e4m3fn), idx, w.sm_scale)
+    assert torch.equal(a, b) and torch.equal(a, c)
+
+
+def test_tuning_kwargs_do_not_change_the_result(cuda_device):
+    w = synthetic.make_host("c1", seed=5)
+    pool = U.device_pool(w.kv_src_bits)
+    q = U.bf16_tensor(w.q_bits)
+    idx = torch.from_numpy(w.slots).cuda()
+    a = fp8_ds_mla_sparse_decode(q, pool, idx, w.sm_scale, block_n=16)
+    b = fp8_ds_mla_sparse_decode(q, pool, idx, w.sm_scale, block_n=32, num_warps=8)
+    assert torch.equal(a, b)
+
+
+def test_out_of_range_indices_issue_no_load(cuda_device):
+    """Indices >= num_slots and < 0 behave as masked (the pool's last row is
+    the boundary; nothing past it is read)."""
+    w = synthetic.make_host("c1", seed=6)
+    pool = U.device_pool(w.kv_src_bits)
+    slots = w.slots.copy()
+    slots[:, ::4] = 4096 + np.arange(slots[:, ::4].size).reshape(slots[:, ::4].shape)
+    slots[:, 1::9] = np.iinfo(np.int32).max
+    slots[:, 2::11] = np.iinfo(np.int32).min
+    q = U.bf16_tensor(w.q_bits)
+    out, lse = _run(q, pool, torch.from_numpy(slots).cuda(), w.sm_scale)
+    ref, ref_lse = O.sparse_decode(synthetic.bf16_to_f32(w.q_bits), pool.view(-1, 656).cpu().numpy(),
+                                   slots, w.sm_scale)
+    U.assert_close(out, ref)
+    U.assert_lse_close(lse, ref_lse)
+
+
+# ------------------------------------------------------------ benchmark shapes
+def _shape_case(name, B, pool_slots, splits=None, seed=0):
+    w = synthetic.make_host(name, seed=seed, B=B, pool_slots=pool_slots)
+    pool = U.device_pool(w.kv_src_bits, check_against_oracle=False)
+    q = U.bf16_tensor(w.q_bits)
+    out, lse = _run(q, pool, torch.from_numpy(w.slots).cuda(), w.sm_scale, num_kv_splits=splits)
+    host_pool = pool.view(-1, 656).cpu().numpy()
+    qf = synthetic.bf16_to_f32(w.q_bits)
+    ref, ref_lse = O.sparse_decode(qf, host_pool, w.slots, w.sm_scale)
+    U.assert_close(out, ref)
+    U.assert_lse_close(lse, ref_lse)
+    ko, _ = O.sparse_decode(qf, host_pool, w.slots, w.sm_scale, kernel_rounding=True)
+    U.assert_close(out, ko, max_abs=U.MAX_ABS_KERNEL_ROUNDING)
+
+
+def test_c2_shape_h128_topk2048(cuda_device):
+    _shape_case("c2", B=4, pool_slots=4 * 32768)
+
+
+def test_c3_shape_h16_eight_splits(cuda_device):
+    _shape_case("c3", B=8, pool_slots=1 << 18, splits=8)
+
+
+def test_c4_shape_h64_edge_cases(cuda_device):
+    # amax spread 1e-4..1e4 + zero tiles, leading 512 masked for 8 requests
+    _shape_case("c4", B=10, pool_slots=10 * 131072)
+
+
+@pytest.mark.parametrize("H", [1, 2, 8, 24, 48, 64, 96, 128, 256])
+def test_head_counts(cuda_device, H):
+    s = synthetic.Shape("h", B=2, H=H, topk=320, ctx=1024, pool_slots=4096, mask_frac=0.1)
+    w = synthetic.make_host(s, seed=H)
+    pool = U.device_pool(w.kv_src_bits, check_against_oracle=False)
+    q = U.bf16_tensor(w.q_bits)
+    out, lse = _run(q, pool, torch.from_numpy(w.slots).cuda(), w.sm_scale)
+    ref, ref_lse = O.sparse_decode(synthetic.bf16_to_f32(w.q_bits),
+                                   pool.view(-1, 656).cpu().numpy(), w.slots, w.sm_scale)
+    U.assert_close(out, ref)
+    U.assert_lse_close(lse, ref_lse)
+
+
+@pytest.mark.parametrize("topk", [1, 16, 63, 64, 65, 200, 2048])
+def test_ragged_topk(cuda_device, topk):
+    s = synthetic.Shape("k", B=3, H=16, topk=topk, ctx=4096, pool_slots=16384)
+    w = synthetic.make_host(s, seed=topk)
+    pool = U.device_pool(w.kv_src_bits, check_against_oracle=False)
+    q = U.bf16_tensor(w.q_bits)
+    for splits in (1, 3):
+        out, lse = _run(q, pool, torch.from_numpy(w.slots).cuda(), w.sm_scale, num_kv_splits=splits)
+        ref, ref_lse = O.sparse_decode(synthetic.bf16_to_f32(w.q_bits),
+                                       pool.view(-1, 656).cpu().numpy(), w.slots, w.sm_scale)
+        U.assert_close(out, ref)
+        U.assert_lse_close(lse, ref_lse)
+
+
+def test_topk_zero_gives_zeros(cuda_device):
+    q = torch.randn(2, 16, 576, device="cuda").bfloat16()
+    pool = torch.zeros(64, 656, dtype=torch.uint8, device="cuda")
+    out, lse = fp8_ds_mla_sparse_decode(q, pool, torch.zeros(2, 0, dtype=torch.int32, device="cuda"),
+                                        0.1, return_lse=True)
+    assert not out.any() and torch.isneginf(lse).all()
+
+
+def test_int64_offsets_past_2_31(cuda_device):
+    """verify/run_all.py:155-185: slot * 656 > 2^31 in a 3.5M-slot pool."""
+    n = 3_500_000
+    kv = torch.zeros(n, 656, dtype=torch.uint8, device="cuda")
+    rng = np.random.default_rng(7)
+    src = synthetic.bf16_bits(rng.standard_normal((2, 576)).astype(np.float32) * 0.5)
+    rows = O.quantize_rows(src)
+    kv[0] = torch.from_numpy(rows[0]).cuda()
+    kv[n - 1] = torch.from_numpy(rows[1]).cuda()
+    q = U.bf16_tensor(synthetic.bf16_bits(rng.standard_normal((1, 16, 576)).astype(np.float32) * 0.5))
+    idx = torch.tensor([[0, n - 1]], dtype=torch.int32, device="cuda")
+    out, lse = _run(q, kv, idx, 576 ** -0.5)
+    host = np.stack([rows[0], rows[1]])
+    ref, ref_lse = O.sparse_decode(q.float().cpu().numpy(), host, np.array([[0, 1]], np.int32),
+                                   576 ** -0.5)
+    del kv
+    torch.cuda.empty_cache()
+    U.assert_close(out, ref)
+    U.assert_lse_close(lse, ref_lse)
+
+
+def test_full_c2_subset_against_oracle(cuda_device):
+    """Full-size c2 (B=64, 2M-slot pool) built on the GPU; 4 requests checked
+    against the oracle, the rest by batch invariance (each request alone gives
+    the same bits as inside the batch)."""
+    w = synthetic.make_device("c2", seed=1)
+    out, lse = fp8_ds_mla_sparse_decode(w.q, w.kv, w.slots, w.sm_scale, return_lse=True)
+    flat = w.kv.view(-1, 656)
+    for b in (0, 17, 40, 63):
+        sl = w.slots[b].long()
+        ok = sl >= 0
+        rows = flat[sl.clamp(min=0)].cpu().numpy()
+        local = np.where(ok.cpu().numpy(), np.arange(sl.numel()), -1).astype(np.int32)
+        ref, ref_lse = O.sparse_decode(w.q[b:b + 1].float().cpu().numpy(), rows, local[None],
+                                       w.sm_scale)
+        U.assert_close(out[b:b + 1].float().cpu().numpy(), ref)
+        U.assert_lse_close(lse[b:b + 1].cpu().numpy(), ref_lse)
+    one = fp8_ds_mla_sparse_decode(w.q[5:6], w.kv, w.slots[5:6], w.sm_scale)
+    assert torch.equal(one, out[5:6])
+    assert torch.isfinite(out.float()).all()
+    del w
+    torch.cuda.empty_cache()
+
+
+def test_output_is_written_on_the_current_stream(cuda_device):
+    w = synthetic.make_host("c1", seed=8)
+    pool = U.device_pool(w.kv_src_bits, check_against_oracle=False)
+    q = U.bf16_tensor(w.q_bits)
+    idx = torch.from_numpy(w.slots).cuda()
+    ref = fp8_ds_mla_sparse_decode(q, pool, idx, w.sm_scale)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        got = fp8_ds_mla_sparse_decode(q, pool, idx, w.sm_scale)
+    s.synchronize()
+    assert torch.equal(ref, got)
+
+
+def test_cuda_graph_capture_replays_identically(cuda_device):
+    w = synthetic.make_host("c1", seed=9)
+    pool = U.device_pool(w.kv_src_bits, check_against_oracle=False)
+    q = U.bf16_tensor(w.q_bits)
+    idx = torch.from_numpy(w.slots).cuda()
+    ws = torch.empty(1 << 22, dtype=torch.uint8, device="cuda")
+    eager = fp8_ds_mla_sparse_decode(q, pool, idx, w.sm_scale, num_kv_splits=4, workspace=ws)
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fp8_ds_mla_sparse_decode(q, pool, idx, w.sm_scale, num_kv_splits=4, workspace=ws)
+        with torch.cuda.graph(g, stream=s):
+            out = fp8_ds_mla_sparse_decode(q, pool, idx, w.sm_scale, num_kv_splits=4, workspace=ws)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+    del g

@@ -1,0 +1,132 @@
+"""GPU parity of the unit kernels: e4m3 decode (all 256 bytes, both methods),
+the fp8_ds_mla cache writer (byte-exact) and the index converter (bit-exact).
+Mirrors tests/test_fp8_dequant.py, tests/test_dequant_triton_cpu.py,
+tests/test_reference_and_metrics.py:26-53 and tests/test_backend_patch.py:184-214
+of the reference."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests import gpu_util as U
+from tests.conftest import golden
+from vllm_fp8kv import synthetic
+from vllm_fp8kv.cache_writer import concat_and_cache_ds_mla, concat_and_cache_mla
+from vllm_fp8kv.fp8_dequant import build_lut, dequant_device, dequant_triton_launch
+from vllm_fp8kv.index_convert import convert_req_index_to_global_index
+
+pytestmark = pytest.mark.gpu
+
+ALL = torch.arange(256, dtype=torch.uint8)
+
+
+def _bits(t):
+    t = t.cpu()
+    return t.view(torch.int16).numpy().view(np.uint16) if t.element_size() == 2 else \
+        t.view(torch.int32).numpy().view(np.uint32)
+
+
+def _assert_bit_exact(got: torch.Tensor, want_bits: np.ndarray, want_f: np.ndarray):
+    g = got.cpu().float().numpy()
+    assert np.array_equal(np.isnan(g), np.isnan(want_f)), "NaN positions differ"
+    ok = np.isnan(want_f) | (_bits(got) == want_bits)
+    assert ok.all(), f"{(~ok).sum()} mismatches at bytes {np.flatnonzero(~ok)[:8]}"
+
+
+@pytest.mark.parametrize("method", [0, 1])
+@pytest.mark.parametrize("dtype,key", [(torch.float16, "f16_bits"), (torch.bfloat16, "bf16_bits"),
+                                       (torch.float32, "f32_bits")])
+def test_dequant_all_256_bytes_bit_exact(cuda_device, method, dtype, key):
+    g = golden("dequant.npz")
+    got = dequant_device(ALL.cuda(), dtype, method)
+    _assert_bit_exact(got, g[key], g["f32_bits"].view(np.float32))
+
+
+def test_dequant_denormals_and_signed_zero(cuda_device):
+    b = torch.tensor([0x01, 0x02, 0x07, 0x80, 0x81, 0x87], dtype=torch.uint8, device="cuda")
+    for method in (0, 1):
+        out = dequant_device(b, torch.float16, method)
+        ref = b.view(torch.float8_e4m3fn).to(torch.float16)
+        assert torch.equal(out, ref)
+        assert torch.signbit(out[3]), "-0.0 lost its sign"
+
+
+@pytest.mark.parametrize("n", [300, 1 << 20])
+def test_dequant_ragged_and_large_random(cuda_device, n):
+    g = torch.Generator().manual_seed(n)
+    u8 = torch.randint(0, 256, (n,), generator=g, dtype=torch.uint8).cuda()
+    lut = build_lut(torch.float16, device="cuda")
+    bm, lt = dequant_triton_launch(u8, lut)
+    ref = u8.view(torch.float8_e4m3fn).to(torch.float16)
+    for got in (bm, lt):
+        assert got.shape == (n,)
+        assert torch.equal(got.isnan(), ref.isnan())
+        keep = ~ref.isnan()
+        assert torch.equal(got[keep].view(torch.int16), ref[keep].view(torch.int16))
+
+
+def test_writer_byte_exact_with_reference_golden(cuda_device):
+    g = golden("writer.npz")
+    kv_c = U.bf16_tensor(g["kv_c_bits"])
+    k_pe = U.bf16_tensor(g["k_pe_bits"])
+    cache = torch.zeros(64, 656, dtype=torch.uint8, device="cuda")
+    concat_and_cache_ds_mla(kv_c, k_pe, cache, torch.from_numpy(g["slots"]).cuda())
+    got = cache.cpu().numpy()
+    diff = np.argwhere(got != g["cache"])
+    assert diff.size == 0, f"{len(diff)} bytes differ, first at {diff[0]}"
+
+
+def test_writer_byte_exact_on_amax_spread_and_zero_tiles(cuda_device):
+    """c4 edge (c): tile amax log-uniform in [1e-4, 1e4] plus exact-zero tiles."""
+    w = synthetic.make_host("c4", seed=2, B=1, pool_slots=8192)
+    U.device_pool(w.kv_src_bits, check_against_oracle=True)
+
+
+def test_writer_skips_padding_and_ignores_k_scale(cuda_device):
+    g = golden("writer.npz")
+    kv_c = U.bf16_tensor(g["kv_c_bits"])
+    k_pe = U.bf16_tensor(g["k_pe_bits"])
+    slots = g["slots"].copy()
+    slots[::3] = -1
+    cache = torch.zeros(64, 656, dtype=torch.uint8, device="cuda")
+    concat_and_cache_mla(kv_c, k_pe, cache, torch.from_numpy(slots).cuda(), "fp8_ds_mla",
+                         torch.tensor(2.0))
+    want = np.zeros_like(g["cache"])
+    O.ds_mla_write(g["kv_c_bits"], g["k_pe_bits"], slots, want)
+    assert np.array_equal(cache.cpu().numpy(), want)
+
+
+def test_writer_strided_inputs(cuda_device):
+    rng = np.random.default_rng(3)
+    src = synthetic.bf16_bits(rng.standard_normal((100, 700)).astype(np.float32))
+    t = U.bf16_tensor(src)
+    kv_c, k_pe = t[:, :512], t[:, 600:664]
+    cache = torch.zeros(2, 64, 656, dtype=torch.uint8, device="cuda")
+    slots = torch.from_numpy(rng.permutation(128)[:100].astype(np.int64)).cuda()
+    concat_and_cache_ds_mla(kv_c, k_pe, cache, slots)
+    want = np.zeros((128, 656), np.uint8)
+    O.ds_mla_write(src[:, :512], src[:, 600:664], slots.cpu().numpy(), want)
+    assert np.array_equal(cache.view(-1, 656).cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("which", ["in_range", "oob"])
+def test_index_converter_matches_vllm(cuda_device, which):
+    g = golden("index.npz")
+    ti = g["token_idx"] if which == "in_range" else g["token_idx_oob"]
+    want = g["out"] if which == "in_range" else g["out_oob"]
+    got = convert_req_index_to_global_index(
+        torch.from_numpy(g["req_id"]).cuda(), torch.from_numpy(g["block_table"]).cuda(),
+        torch.from_numpy(ti).cuda(), BLOCK_SIZE=int(g["block_size"]), NUM_TOPK_TOKENS=ti.shape[1])
+    assert np.array_equal(got.cpu().numpy(), want)
+
+
+def test_index_converter_large_random_vs_oracle(cuda_device):
+    rng = np.random.default_rng(4)
+    T, R, nb, topk = 512, 64, 512, 2048
+    req = rng.integers(0, R, T).astype(np.int32)
+    bt = rng.integers(0, 1 << 16, (R, nb)).astype(np.int32)
+    ti = rng.integers(-1, nb * 64 + 100, (T, topk)).astype(np.int32)
+    got = convert_req_index_to_global_index(torch.from_numpy(req).cuda(), torch.from_numpy(bt).cuda(),
+                                            torch.from_numpy(ti).cuda(), 64, topk)
+    assert np.array_equal(got.cpu().numpy(), O.convert_req_index(req, bt, ti, 64))

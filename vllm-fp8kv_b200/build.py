@@ -1,0 +1,67 @@
+"""Build libfp8mla.so (sm_100a) in-tree: vllm-fp8kv_b200/vllm_fp8kv/libfp8mla.so.
+
+    python vllm-fp8kv_b200/build.py [--verbose-ptxas]
+
+nvcc cross-compiles without a GPU.  Every translation unit is compiled with
+``-gencode arch=compute_100a,code=sm_100a -lineinfo -O3`` and linked into one
+shared library with a static CUDA runtime; the C ABI is include/fp8mla.h.
+"""
+
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+OUT_DIR = os.path.join(HERE, "vllm_fp8kv")
+LIB = os.path.join(OUT_DIR, "libfp8mla.so")
+OBJ_DIR = os.path.join(HERE, "_build")
+SOURCES = ["abi.cu", "unit_kernels.cu", "decode_mma.cu", "decode_tc.cu"]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def _compile(src: str, verbose_ptxas: bool) -> str:
+    obj = os.path.join(OBJ_DIR, src.replace(".cu", ".o"))
+    cmd = [nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
+           "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr",
+           "-DNDEBUG", "-c", os.path.join(CSRC, src), "-o", obj]
+    if verbose_ptxas:
+        cmd += ["-Xptxas", "-v"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {src}:\n{r.stdout}\n{r.stderr}")
+    if verbose_ptxas:
+        sys.stderr.write(r.stderr)
+    return obj
+
+
+def build(verbose_ptxas: bool = False) -> str:
+    os.makedirs(OBJ_DIR, exist_ok=True)
+    with cf.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
+        objs = list(ex.map(lambda s: _compile(s, verbose_ptxas), SOURCES))
+    tmp = LIB + ".tmp"
+    cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-cudart", "static"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--verbose-ptxas", action="store_true")
+    args = ap.parse_args()
+    print(build(args.verbose_ptxas))

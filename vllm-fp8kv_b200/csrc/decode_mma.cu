@@ -1,0 +1,338 @@
+// decode_mma.cu -- split-KV sparse MLA decode over fp8_ds_mla pages for any
+// head count (the general path; H = 128 uses the tcgen05 kernel of
+// decode_tc.cu), plus the LSE merge of the split partials.
+//
+// One CTA = (query token, block of <= 16 heads, split of the top-k axis).
+// Per 64-token chunk:
+//   gather   4 threads per row issue 41 x 16-byte cp.async (zero-fill for
+//            masked slots: no global read), double-buffered;
+//   dequant  one warp per row: e4m3 * tile scale -> bf16 (bit-math, exact
+//            fp32 product then RNE, as the reference: decode.py:152-164);
+//   QK^T     8 warps x 8 tokens x 36 k-steps of m16n8k16 (d = 576);
+//   softmax  exp2 online softmax; a still -inf running max is replaced by 0
+//            so a fully masked chunk contributes nothing (decode.py:178-197);
+//   PV       8 warps x 64 output dims, V = the dequantized NoPE rows.
+// Reference semantics: vllm_fp8kv/fp8_ds_mla_sparse_decode.py:77-211 and the
+// split/merge pair of tests/fixtures/triton_mla_sparse_kernel_pr47629.py:232-403.
+#include "common.cuh"
+#include "decode.h"
+
+namespace fp8mla {
+
+namespace {
+
+constexpr int kBN = 64;         // tokens per chunk
+constexpr int kBH = 16;         // heads per CTA
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kKStride = 584;   // bf16 per sQ / sK row: 576 + 8 (1168 B = 73 x 16 B)
+constexpr int kPStride = kBN + 8;
+
+struct Smem {
+  uint16_t q[kBH * kKStride];
+  uint16_t k[kBN * kKStride];
+  uint8_t raw[2][kBN * kRowBytes];
+  uint16_t p[kBH * kPStride];
+  float red_max[kWarps][kBH];
+  float red_sum[kWarps][kBH];
+  int valid[2][kBN];
+};
+static_assert(sizeof(Smem) <= 227 * 1024, "shared memory budget");
+static_assert(offsetof(Smem, raw) % 16 == 0, "cp.async destinations must be 16-B aligned");
+
+__device__ __forceinline__ void issue_gather(Smem& s, int buf, const DecodeArgs& a,
+                                             const int32_t* idx_row, int pos0, int end) {
+  const int r = threadIdx.x >> 2, sub = threadIdx.x & 3;
+  const int pos = pos0 + r;
+  int64_t slot = -1;
+  if (pos < end) {
+    int32_t v = idx_row[pos];
+    if (v >= 0 && (int64_t)v < a.num_slots) slot = v;
+  }
+  const bool ok = slot >= 0;
+  const uint8_t* src = a.kv + (ok ? slot : 0) * (int64_t)kRowBytes;
+  const uint32_t dst = smem_u32(&s.raw[buf][r * kRowBytes]);
+  for (int j = sub; j < kRowChunks16; j += 4) cp_async16(dst + j * 16, src + j * 16, ok ? 16 : 0);
+  if (sub == 0) s.valid[buf][r] = ok;
+}
+
+}  // namespace
+
+template <typename QT, typename OT>
+__global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const DecodeArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  const int nhb = a.G * a.hb_per_group;                    // head blocks per token
+  const int hbi = blockIdx.x % nhb;
+  const int grp = hbi / a.hb_per_group;
+  const int hb = hbi % a.hb_per_group;
+  const int hrow0 = hb * a.block_h;                        // head offset within group
+  const int nh = min(a.block_h, a.hpg - hrow0);            // valid heads in this CTA
+  const int head0 = grp * a.hpg + hrow0;
+  const int64_t t = blockIdx.x / nhb;
+  const int split = blockIdx.y;
+  const int beg = split * a.split_len;
+  const int end = min(a.topk, beg + a.split_len);
+  const int32_t* idx_row = a.idx + t * a.idx_st + grp * a.idx_sg;
+
+  // ---- Q -> smem (bf16), zero rows for padded heads
+  for (int e = tid; e < kBH * (kDqk / 8); e += kThreads) {
+    const int row = e / (kDqk / 8), c8 = e % (kDqk / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < nh) {
+      const QT* src = static_cast<const QT*>(a.q) + t * a.q_st + (int64_t)(head0 + row) * a.q_sh + c8 * 8;
+      if constexpr (sizeof(QT) == 2) {
+        v = *reinterpret_cast<const uint4*>(src);
+      } else {
+        const float4 f0 = reinterpret_cast<const float4*>(src)[0];
+        const float4 f1 = reinterpret_cast<const float4*>(src)[1];
+        v = make_uint4(pack_bf16x2(f0.x, f0.y), pack_bf16x2(f0.z, f0.w),
+                       pack_bf16x2(f1.x, f1.y), pack_bf16x2(f1.z, f1.w));
+      }
+    }
+    *reinterpret_cast<uint4*>(&s.q[row * kKStride + c8 * 8]) = v;
+  }
+
+  const int nchunks = end > beg ? (end - beg + kBN - 1) / kBN : 0;
+  if (nchunks > 0) issue_gather(s, 0, a, idx_row, beg, end);
+  cp_async_commit();
+  if (nchunks > 1) issue_gather(s, 1, a, idx_row, beg + kBN, end);
+  cp_async_commit();
+
+  const int g = lane >> 2, q4 = lane & 3;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_part[2] = {0.f, 0.f};
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+
+  const uint32_t q_base = smem_u32(s.q);
+  const uint32_t k_base = smem_u32(s.k);
+  const uint32_t p_base = smem_u32(s.p);
+
+  for (int c = 0; c < nchunks; ++c) {
+    const int buf = c & 1;
+    cp_async_wait<1>();
+    __syncthreads();
+    // validity of this thread's two score columns, read before the gather of
+    // chunk c + 2 reuses the flag buffer
+    const int col = warp * 8 + q4 * 2;
+    const bool v0 = s.valid[buf][col] != 0, v1 = s.valid[buf][col + 1] != 0;
+
+    // ---- dequant raw[buf] -> k (bf16): warp per row, lane owns 16 bytes
+    for (int r = warp; r < kBN; r += kWarps) {
+      const uint8_t* row = &s.raw[buf][r * kRowBytes];
+      const uint4 w = reinterpret_cast<const uint4*>(row)[lane];
+      const float sc = reinterpret_cast<const float*>(row + kScaleOff)[lane >> 3];
+      float sx;
+      bool fused;
+      prep_scale(sc, sx, fused);
+      uint4 o0, o1;
+      dequant4_bf16(w.x, sx, fused, o0.x, o0.y);
+      dequant4_bf16(w.y, sx, fused, o0.z, o0.w);
+      dequant4_bf16(w.z, sx, fused, o1.x, o1.y);
+      dequant4_bf16(w.w, sx, fused, o1.z, o1.w);
+      uint4* dst = reinterpret_cast<uint4*>(&s.k[r * kKStride + lane * 16]);
+      dst[0] = o0;
+      dst[1] = o1;
+      if (lane < 8)
+        reinterpret_cast<uint4*>(&s.k[r * kKStride + kNope])[lane] =
+            reinterpret_cast<const uint4*>(row + kRopeOff)[lane];
+    }
+    __syncthreads();
+    if (c + 2 < nchunks) issue_gather(s, buf, a, idx_row, beg + (c + 2) * kBN, end);
+    cp_async_commit();
+
+    // ---- S = Q K^T for this warp's 8 tokens
+    const int n0 = warp * 8;
+    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 6
+    for (int kk = 0; kk < kDqk / 16; kk += 2) {
+      uint32_t a0, a1, a2, a3, a4, a5, a6, a7, b0, b1, b2, b3;
+      const uint32_t qa = q_base + (((lane & 15) * kKStride + kk * 16 + (lane >> 4) * 8) << 1);
+      ldmatrix_x4(qa, a0, a1, a2, a3);
+      ldmatrix_x4(qa + 32, a4, a5, a6, a7);
+      const uint32_t kb = k_base + (((n0 + (lane & 7)) * kKStride + kk * 16 + (lane >> 3) * 8) << 1);
+      ldmatrix_x4(kb, b0, b1, b2, b3);
+      mma_bf16_16816(sacc, a0, a1, a2, a3, b0, b1);
+      mma_bf16_16816(sacc, a4, a5, a6, a7, b2, b3);
+    }
+
+    // ---- online softmax (exp2 form)
+    float x[4];
+    x[0] = (v0 && g < nh) ? sacc[0] * a.scale_log2 : -INFINITY;
+    x[1] = (v1 && g < nh) ? sacc[1] * a.scale_log2 : -INFINITY;
+    x[2] = (v0 && g + 8 < nh) ? sacc[2] * a.scale_log2 : -INFINITY;
+    x[3] = (v1 && g + 8 < nh) ? sacc[3] * a.scale_log2 : -INFINITY;
+    float mt0 = fmaxf(x[0], x[1]), mt1 = fmaxf(x[2], x[3]);
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) {
+      mt0 = fmaxf(mt0, __shfl_xor_sync(0xFFFFFFFFu, mt0, o));
+      mt1 = fmaxf(mt1, __shfl_xor_sync(0xFFFFFFFFu, mt1, o));
+    }
+    if (q4 == 0) {
+      s.red_max[warp][g] = mt0;
+      s.red_max[warp][g + 8] = mt1;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      mt0 = fmaxf(mt0, s.red_max[w][g]);
+      mt1 = fmaxf(mt1, s.red_max[w][g + 8]);
+    }
+    float alpha[2], safe[2];
+    const float mn[2] = {fmaxf(m_run[0], mt0), fmaxf(m_run[1], mt1)};
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      safe[i] = (mn[i] == -INFINITY) ? 0.f : mn[i];
+      alpha[i] = exp2f(m_run[i] - safe[i]);
+      m_run[i] = mn[i];
+    }
+    const float p0 = exp2f(x[0] - safe[0]), p1 = exp2f(x[1] - safe[0]);
+    const float p2 = exp2f(x[2] - safe[1]), p3 = exp2f(x[3] - safe[1]);
+    l_part[0] = l_part[0] * alpha[0] + p0 + p1;
+    l_part[1] = l_part[1] * alpha[1] + p2 + p3;
+    *reinterpret_cast<uint32_t*>(&s.p[g * kPStride + col]) = pack_bf16x2(p0, p1);
+    *reinterpret_cast<uint32_t*>(&s.p[(g + 8) * kPStride + col]) = pack_bf16x2(p2, p3);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      acc[i][0] *= alpha[0];
+      acc[i][1] *= alpha[0];
+      acc[i][2] *= alpha[1];
+      acc[i][3] *= alpha[1];
+    }
+    __syncthreads();
+
+    // ---- O += P V for this warp's 64 output dims
+    const int d0 = warp * 64;
+#pragma unroll
+    for (int kk = 0; kk < kBN / 16; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      ldmatrix_x4(p_base + (((lane & 15) * kPStride + kk * 16 + (lane >> 4) * 8) << 1), a0, a1, a2, a3);
+#pragma unroll
+      for (int nt = 0; nt < 8; nt += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int tok = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        ldmatrix_x4_trans(k_base + ((tok * kKStride + d0 + nt * 8 + (lane >> 4) * 8) << 1), b0, b1, b2, b3);
+        mma_bf16_16816(acc[nt], a0, a1, a2, a3, b0, b1);
+        mma_bf16_16816(acc[nt + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+  }
+  cp_async_wait<0>();
+
+  // ---- row sums across the quad and the 8 warps
+#pragma unroll
+  for (int o = 1; o < 4; o <<= 1) {
+    l_part[0] += __shfl_xor_sync(0xFFFFFFFFu, l_part[0], o);
+    l_part[1] += __shfl_xor_sync(0xFFFFFFFFu, l_part[1], o);
+  }
+  __syncthreads();
+  if (q4 == 0) {
+    s.red_sum[warp][g] = l_part[0];
+    s.red_sum[warp][g + 8] = l_part[1];
+  }
+  __syncthreads();
+  float l[2] = {0.f, 0.f};
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    l[0] += s.red_sum[w][g];
+    l[1] += s.red_sum[w][g + 8];
+  }
+
+  const int d0 = warp * 64 + q4 * 2;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int row = g + half * 8;
+    if (row >= nh) continue;
+    const int h = head0 + row;
+    const float inv = l[half] > 0.f ? 1.f / l[half] : 1.f;
+    const float lse_v = l[half] > 0.f ? m_run[half] * kLn2 + logf(l[half]) : -INFINITY;
+    if (a.num_splits == 1) {
+      OT* o = static_cast<OT*>(a.out) + t * a.out_st + (int64_t)h * a.out_sh + d0;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const float v0 = acc[nt][half * 2] * inv, v1 = acc[nt][half * 2 + 1] * inv;
+        if constexpr (sizeof(OT) == 2) {
+          *reinterpret_cast<uint32_t*>(o + nt * 8) = pack_bf16x2(v0, v1);
+        } else {
+          *reinterpret_cast<float2*>(o + nt * 8) = make_float2(v0, v1);
+        }
+      }
+      if (a.lse != nullptr && warp == 0 && q4 == 0) a.lse[t * a.lse_st + h] = lse_v;
+    } else {
+      const int64_t base = ((t * a.H + h) * a.num_splits + split);
+      float* o = a.ws_o + base * kNope + d0;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+        *reinterpret_cast<float2*>(o + nt * 8) =
+            make_float2(acc[nt][half * 2] * inv, acc[nt][half * 2 + 1] * inv);
+      if (warp == 0 && q4 == 0) a.ws_lse[base] = lse_v;
+    }
+  }
+}
+
+// LSE merge of split partials: out = sum_s w_s o_s / sum_s w_s with
+// w_s = exp(lse_s - max lse); an all-empty row gives zeros and LSE -inf.
+// Reference: tests/fixtures/triton_mla_sparse_kernel_pr47629.py:331-403.
+template <typename OT>
+__global__ void __launch_bounds__(128) merge_splits_kernel(const DecodeArgs a) {
+  const int64_t th = blockIdx.x;  // t * H + h
+  const int64_t t = th / a.H, h = th % a.H;
+  const int S = a.num_splits;
+  const float* lse_s = a.ws_lse + th * S;
+  float m = -INFINITY;
+  for (int i = 0; i < S; ++i) m = fmaxf(m, lse_s[i]);
+  const int d = threadIdx.x * 4;
+  float4 accv = make_float4(0.f, 0.f, 0.f, 0.f);
+  float denom = 0.f;
+  if (m != -INFINITY) {
+    for (int i = 0; i < S; ++i) {
+      const float w = expf(lse_s[i] - m);
+      denom += w;
+      const float4 o = *reinterpret_cast<const float4*>(a.ws_o + (th * S + i) * kNope + d);
+      accv.x += w * o.x;
+      accv.y += w * o.y;
+      accv.z += w * o.z;
+      accv.w += w * o.w;
+    }
+  }
+  const float inv = denom > 0.f ? 1.f / denom : 1.f;
+  OT* o = static_cast<OT*>(a.out) + t * a.out_st + h * a.out_sh + d;
+  if constexpr (sizeof(OT) == 2) {
+    reinterpret_cast<uint2*>(o)[0] =
+        make_uint2(pack_bf16x2(accv.x * inv, accv.y * inv), pack_bf16x2(accv.z * inv, accv.w * inv));
+  } else {
+    reinterpret_cast<float4*>(o)[0] = make_float4(accv.x * inv, accv.y * inv, accv.z * inv, accv.w * inv);
+  }
+  if (a.lse != nullptr && threadIdx.x == 0)
+    a.lse[t * a.lse_st + h] = denom > 0.f ? m + logf(denom) : -INFINITY;
+}
+
+int launch_decode_mma(const DecodeArgs& a, cudaStream_t st) {
+  const size_t smem = sizeof(Smem);
+  // head blocks of one token are adjacent in x so they re-hit the same rows in L2
+  dim3 grid((unsigned)(a.T * a.G * a.hb_per_group), a.num_splits);
+  int rc = FP8MLA_OK;
+  auto go = [&](auto kern) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return check_cuda(e, "decode_mma smem attribute");
+    kern<<<grid, kThreads, smem, st>>>(a);
+    return check_cuda(cudaGetLastError(), "decode_mma_kernel launch");
+  };
+  if (a.q_dtype == FP8MLA_DTYPE_BF16)
+    rc = go(decode_mma_kernel<__nv_bfloat16, __nv_bfloat16>);
+  else
+    rc = go(decode_mma_kernel<float, float>);
+  if (rc != FP8MLA_OK || a.num_splits == 1) return rc;
+  dim3 mgrid((unsigned)(a.T * a.H));
+  if (a.q_dtype == FP8MLA_DTYPE_BF16)
+    merge_splits_kernel<__nv_bfloat16><<<mgrid, 128, 0, st>>>(a);
+  else
+    merge_splits_kernel<float><<<mgrid, 128, 0, st>>>(a);
+  return check_cuda(cudaGetLastError(), "merge_splits_kernel launch");
+}
+
+}  // namespace fp8mla

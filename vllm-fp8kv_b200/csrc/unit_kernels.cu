@@ -1,0 +1,222 @@
+// unit_kernels.cu -- the small kernels around the decode:
+//   * e4m3fn byte decode (unit test of the fused decode's dequant),
+//   * the fp8_ds_mla cache writer,
+//   * the block-table -> flat slot index converter.
+// All are HBM-bound integer/byte work; grids are sized in multiples of the SM
+// count and every access is coalesced 16-byte or 4-byte traffic.
+#include "common.cuh"
+
+namespace fp8mla {
+
+// ============================================================= e4m3 decode
+// Reference: vllm_fp8kv/fp8_dequant.py:80-113 (`dequant_bitmath_triton`,
+// `_dequant_test_kernel`).  method 0: packed hardware cvt e4m3x2 -> f16x2;
+// method 1: the integer bit-math of dequant4_bf16 (scale 1).
+template <int kOut>  // FP8MLA_DTYPE_*
+__global__ void dequant_e4m3_kernel(const uint8_t* __restrict__ in, int64_t n,
+                                    void* __restrict__ out, int method) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    uint32_t b = in[i];
+    float v;
+    if (method == 0) {
+      uint32_t h2;
+      uint16_t pair = (uint16_t)b;
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;\n" : "=r"(h2) : "h"(pair));
+      __half h = __ushort_as_half((unsigned short)(h2 & 0xFFFFu));
+      if (kOut == FP8MLA_DTYPE_F16) {
+        static_cast<__half*>(out)[i] = h;
+        continue;
+      }
+      v = __half2float(h);
+    } else {
+      uint32_t lo, hi;
+      dequant4_bf16(b, 1.0f, false, lo, hi);  // exact: every e4m3 value fits bf16
+      v = e4m3_to_f32(b);
+      if (kOut == FP8MLA_DTYPE_BF16) {
+        static_cast<uint16_t*>(out)[i] = (uint16_t)(lo & 0xFFFFu);
+        continue;
+      }
+    }
+    if (kOut == FP8MLA_DTYPE_F32) {
+      static_cast<float*>(out)[i] = v;
+    } else if (kOut == FP8MLA_DTYPE_F16) {
+      static_cast<__half*>(out)[i] = __float2half_rn(v);
+    } else {
+      static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// ============================================================= cache writer
+// fp32 -> e4m3fn byte with torch's semantics (round to nearest even; values
+// that round past 448, inf and NaN give 0x7F | sign).  Written from the IEEE
+// definition; the CPU oracle states the same rule.
+__device__ __forceinline__ uint32_t f32_to_e4m3(float x) {
+  uint32_t u = __float_as_uint(x);
+  uint32_t sign = (u >> 24) & 0x80u;
+  uint32_t a = u & 0x7FFFFFFFu;
+  uint32_t r;
+  if (a >= 0x43F00000u) {  // >= 480, inf, NaN
+    r = 0x7Fu;
+  } else if (a < 0x3C800000u) {  // < 2^-6: subnormal range, units of 2^-9
+    r = (uint32_t)__float2int_rn(__uint_as_float(a) * 512.0f);
+  } else {
+    uint32_t e = (a >> 23) - 127u + 7u;
+    uint32_t mant = a & 0x7FFFFFu;
+    uint32_t keep = mant >> 20, rem = mant & 0xFFFFFu;
+    keep += (rem > 0x80000u || (rem == 0x80000u && (keep & 1u))) ? 1u : 0u;
+    r = (e << 3) + keep;  // a carry out of the mantissa bumps the exponent
+  }
+  return r | sign;
+}
+
+// One warp per token: lane l owns latent elements [16l, 16l+16) (tile l/8),
+// reduces amax over its tile with 8-lane shuffles, divides, converts, and
+// writes 16 bytes; lanes 0..3 write the 4 scales, lanes 0..7 copy the rope.
+// Reference semantics: tests/fakes.py:28-57, verify/reference.py:68-91.
+__global__ void __launch_bounds__(256) ds_mla_write_kernel(
+    const uint16_t* __restrict__ kv_c, int64_t kv_c_stride, const uint16_t* __restrict__ k_pe,
+    int64_t k_pe_stride, const int64_t* __restrict__ slot_mapping, int64_t N,
+    uint8_t* __restrict__ cache, int64_t num_slots) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t tok = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; tok < N;
+       tok += warps_total) {
+    const int64_t slot = slot_mapping[tok];
+    if (slot < 0 || slot >= num_slots) continue;  // padding token
+    const uint16_t* src = kv_c + tok * kv_c_stride + lane * 16;
+    uint32_t w[8];
+    if ((kv_c_stride % 8) == 0 && (reinterpret_cast<uintptr_t>(kv_c) & 15) == 0) {
+      uint4 a = reinterpret_cast<const uint4*>(src)[0];
+      uint4 b = reinterpret_cast<const uint4*>(src)[1];
+      w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+      w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = (uint32_t)src[2 * j] | ((uint32_t)src[2 * j + 1] << 16);
+    }
+    float x[16];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      x[2 * j] = bf16_lo(w[j]);
+      x[2 * j + 1] = bf16_hi(w[j]);
+    }
+    // amax over the tile (NaN sticky, as torch's amax)
+    float amax = 0.0f;
+    bool nan = false;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float v = fabsf(x[j]);
+      nan |= (v != v);
+      amax = fmaxf(amax, v);
+    }
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) {
+      amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
+      nan |= __shfl_xor_sync(0xFFFFFFFFu, (int)nan, off) != 0;
+    }
+    float scale = nan ? __uint_as_float(0x7FC00000u) : __fdiv_rn(amax, 448.0f);
+    if (!nan && scale < 1.1754944e-38f) scale = 1.1754944e-38f;
+    uint32_t q[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t b0 = f32_to_e4m3(__fdiv_rn(x[4 * j + 0], scale));
+      uint32_t b1 = f32_to_e4m3(__fdiv_rn(x[4 * j + 1], scale));
+      uint32_t b2 = f32_to_e4m3(__fdiv_rn(x[4 * j + 2], scale));
+      uint32_t b3 = f32_to_e4m3(__fdiv_rn(x[4 * j + 3], scale));
+      q[j] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    }
+    uint8_t* row = cache + slot * (int64_t)kRowBytes;
+    reinterpret_cast<uint4*>(row)[lane] = make_uint4(q[0], q[1], q[2], q[3]);
+    if ((lane & 7) == 0) reinterpret_cast<float*>(row + kScaleOff)[lane >> 3] = scale;
+    if (lane < 8) {
+      const uint16_t* r = k_pe + tok * k_pe_stride + lane * 8;
+      uint32_t p[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) p[j] = (uint32_t)r[2 * j] | ((uint32_t)r[2 * j + 1] << 16);
+      reinterpret_cast<uint4*>(row + kRopeOff)[lane] = make_uint4(p[0], p[1], p[2], p[3]);
+    }
+  }
+}
+
+// ============================================================= index convert
+// out[t, i] = block_table[req_id[t], tok / B] * B + tok % B; -1 when tok < 0 or
+// the block index is outside [0, max_blocks).  int32 arithmetic, as vLLM's
+// converter (installed vllm/v1/attention/backends/mla/sparse_utils.py:11-78).
+__global__ void convert_req_index_kernel(const int32_t* __restrict__ req_id,
+                                         const int32_t* __restrict__ block_table,
+                                         int64_t bt_stride, int64_t max_blocks,
+                                         const int32_t* __restrict__ token_idx,
+                                         int64_t ti_stride, int64_t T, int64_t topk,
+                                         int32_t block_size, int32_t* __restrict__ out,
+                                         int64_t out_stride) {
+  const int64_t total = T * topk;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+    const int64_t t = e / topk, i = e - t * topk;
+    const int32_t tok = token_idx[t * ti_stride + i];
+    int32_t r = -1;
+    if (tok >= 0) {
+      const int32_t blk = tok / block_size, off = tok - blk * block_size;
+      if (blk < max_blocks) {
+        const uint32_t base = (uint32_t)block_table[(int64_t)req_id[t] * bt_stride + blk];
+        r = (int32_t)(base * (uint32_t)block_size + (uint32_t)off);
+      }
+    }
+    out[t * out_stride + i] = r;
+  }
+}
+
+// ============================================================= launchers
+static int grid_for(int64_t work, int block) {
+  int64_t sms = device_sm_count();
+  int64_t want = (work + block - 1) / block;
+  int64_t cap = sms * 16;
+  if (want > cap) want = cap;
+  return (int)(want < 1 ? 1 : want);
+}
+
+int launch_dequant(const uint8_t* in, int64_t n, void* out, int out_dtype, int method,
+                   cudaStream_t st) {
+  if (n == 0) return FP8MLA_OK;
+  const int block = 256;
+  const int grid = grid_for(n, block);
+  switch (out_dtype) {
+    case FP8MLA_DTYPE_F16:
+      dequant_e4m3_kernel<FP8MLA_DTYPE_F16><<<grid, block, 0, st>>>(in, n, out, method);
+      break;
+    case FP8MLA_DTYPE_BF16:
+      dequant_e4m3_kernel<FP8MLA_DTYPE_BF16><<<grid, block, 0, st>>>(in, n, out, method);
+      break;
+    default:
+      dequant_e4m3_kernel<FP8MLA_DTYPE_F32><<<grid, block, 0, st>>>(in, n, out, method);
+  }
+  return check_cuda(cudaGetLastError(), "dequant_e4m3_kernel launch");
+}
+
+int launch_ds_mla_write(const uint16_t* kv_c, int64_t kv_c_stride, const uint16_t* k_pe,
+                        int64_t k_pe_stride, const int64_t* slot_mapping, int64_t N,
+                        uint8_t* cache, int64_t num_slots, cudaStream_t st) {
+  if (N == 0) return FP8MLA_OK;
+  const int block = 256;  // 8 tokens per block
+  const int grid = grid_for(N * 32, block);
+  ds_mla_write_kernel<<<grid, block, 0, st>>>(kv_c, kv_c_stride, k_pe, k_pe_stride,
+                                              slot_mapping, N, cache, num_slots);
+  return check_cuda(cudaGetLastError(), "ds_mla_write_kernel launch");
+}
+
+int launch_convert_req_index(const int32_t* req_id, const int32_t* block_table,
+                             int64_t bt_stride, int64_t max_blocks, const int32_t* token_idx,
+                             int64_t ti_stride, int64_t T, int64_t topk, int64_t block_size,
+                             int32_t* out, int64_t out_stride, cudaStream_t st) {
+  if (T * topk == 0) return FP8MLA_OK;
+  const int block = 256;
+  const int grid = grid_for(T * topk, block);
+  convert_req_index_kernel<<<grid, block, 0, st>>>(req_id, block_table, bt_stride, max_blocks,
+                                                   token_idx, ti_stride, T, topk,
+                                                   (int32_t)block_size, out, out_stride);
+  return check_cuda(cudaGetLastError(), "convert_req_index_kernel launch");
+}
+
+}  // namespace fp8mla

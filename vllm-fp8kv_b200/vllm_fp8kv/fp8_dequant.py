@@ -1,0 +1,63 @@
+"""fp8e4m3fn -> fp16/bf16/fp32 decode.
+
+Same surface as the reference module (vllm_fp8kv/fp8_dequant.py:47-113):
+
+* ``dequant_bitmath_torch`` -- the pure-torch bit-math decode (a host-side
+  reference helper; the product kernels never call it);
+* ``build_lut`` -- a 256-entry decode table built with torch's own cast;
+* ``dequant_device`` -- the sm_100a decode kernel: method 0 is the packed
+  hardware conversion (cvt e4m3x2 -> f16x2), method 1 the integer bit-math
+  the fused decode uses (byte magnitude placed in fp32 bits [26:20] gives the
+  value times 2^-120, rescaled exactly);
+* ``dequant_triton_launch`` -- the reference's test driver name, kept for
+  callers: returns (bit-math fp16, table-dtype decode) computed on device.
+
+All of them are exact for every finite byte; 0x7F / 0xFF decode to NaN (the
+payload differs between torch's CPU and CUDA casts, so compare NaN-ness).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from vllm_fp8kv import _native as N
+
+FP16_NAN_MAG = 0x7F80
+
+_DT = {torch.float16: N.DTYPE_F16, torch.bfloat16: N.DTYPE_BF16, torch.float32: N.DTYPE_F32}
+
+
+def dequant_bitmath_torch(u8: torch.Tensor, dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """Torch bit-math decode: fp16((s << 15) | ((b & 0x7F) << 7)) * 256, NaN for 0x7F/0xFF."""
+    assert u8.dtype == torch.uint8
+    b = u8.to(torch.int16)
+    sign = (b & 0x80) << 8
+    h = (sign | ((b & 0x7F) << 7)).view(torch.float16) * 256.0
+    nan = (sign | FP16_NAN_MAG).view(torch.float16)
+    out = torch.where((b & 0x7F) == 0x7F, nan, h)
+    return out if dtype == torch.float16 else out.to(dtype)
+
+
+def build_lut(dtype: torch.dtype = torch.float16, device="cuda") -> torch.Tensor:
+    """256-entry table lut[b] = float8_e4m3fn(b) as `dtype` (torch's own cast)."""
+    return (torch.arange(256, dtype=torch.uint8, device=device)
+            .view(torch.float8_e4m3fn).to(dtype).contiguous())
+
+
+def dequant_device(u8: torch.Tensor, dtype: torch.dtype = torch.float16,
+                   method: int = 0) -> torch.Tensor:
+    """Decode a uint8 CUDA tensor of e4m3fn bytes with the sm_100a kernel."""
+    assert u8.dtype == torch.uint8
+    assert dtype in _DT, dtype
+    N.require_cuda(u8)
+    src = u8.contiguous().reshape(-1)
+    out = torch.empty(src.shape, dtype=dtype, device=u8.device)
+    rc = N.lib().fp8mla_dequant_e4m3(src.data_ptr(), src.numel(), out.data_ptr(), _DT[dtype],
+                                     method, N.stream_ptr(u8.device))
+    N.check(rc, "fp8mla_dequant_e4m3")
+    return out.reshape(u8.shape)
+
+
+def dequant_triton_launch(u8: torch.Tensor, lut: torch.Tensor):
+    """Reference-compatible driver: (bit-math decode as fp16, decode in lut.dtype)."""
+    return dequant_device(u8, torch.float16, method=1), dequant_device(u8, lut.dtype, method=0)

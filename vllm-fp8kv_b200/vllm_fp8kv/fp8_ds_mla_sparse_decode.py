@@ -1,0 +1,125 @@
+"""Sparse-MLA decode over fp8_ds_mla KV pages on B200 (sm_100a).
+
+Drop-in for the reference entry point of the same name
+(vllm_fp8kv/fp8_ds_mla_sparse_decode.py:214-288): same signature, same
+asserts, same outputs.  The work runs in libfp8mla.so:
+
+* H/G == 128 heads per kv group, bf16 q: the tcgen05/TMEM kernel (heads are
+  the MMA M dimension; QK^T over d=576 and PV over d_v=512 on the 5th-gen
+  tensor cores, accumulators in tensor memory);
+* any other head count: the split-KV warp-MMA kernel.
+
+Both gather 656-byte rows by flat slot with 64-bit offsets, issue no load for
+masked slots (index < 0 or >= num_slots), dequantize e4m3 * tile scale to
+bf16 exactly as the reference does, and merge top-k splits by LSE with no NaN
+on fully masked chunks.
+
+fp8_ds_mla row (656 B/token):
+    [  0:512)  512 x fp8e4m3   NoPE latent (kv_lora_rank)
+    [512:528)    4 x fp32      per-128-element tile scales (amax / 448)
+    [528:656)   64 x bf16      RoPE, stored raw
+MLA shares K and V: V is the NoPE half of the same row.  Only the inline tile
+scales are applied (the layer's k_scale is not part of this format).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from vllm_fp8kv import _native as N
+
+NOPE = 512      # kv_lora_rank
+ROPE = 64       # qk_rope_head_dim
+TILE = 128      # elements per fp32 scale
+ROW_BYTES = NOPE + (NOPE // TILE) * 4 + ROPE * 2   # 656
+SCALE_OFF = NOPE                                   # 512
+ROPE_OFF = NOPE + (NOPE // TILE) * 4               # 528
+
+
+def decode_workspace_bytes(T: int, H: int, G: int, topk: int, num_splits: int = 0) -> int:
+    """Device workspace one call needs (0 for a single split)."""
+    return int(N.lib().fp8mla_decode_workspace_bytes(T, H, G, topk, num_splits))
+
+
+def choose_num_kv_splits(T: int, H: int, G: int, topk: int, sm_count: int) -> int:
+    """Split count the decode picks when num_kv_splits is None / 0."""
+    return int(N.lib().fp8mla_choose_num_splits(T, H, G, topk, sm_count))
+
+
+def decode_kernel_name(T: int, H: int, G: int, topk: int, q_dtype=torch.bfloat16,
+                       num_splits: int = 0) -> str:
+    """The kernel(s) one call with this shape dispatches to (introspection)."""
+    code = N.DTYPE_BF16 if q_dtype == torch.bfloat16 else N.DTYPE_F32
+    return N.lib().fp8mla_decode_kernel_name(T, H, G, topk, code, num_splits).decode()
+
+
+def fp8_ds_mla_sparse_decode(
+    q: torch.Tensor,            # [seq_q, h_q, 576]  bf16 (fp32 allowed for tests)
+    kv_cache: torch.Tensor,     # [..., 656] uint8 or float8_e4m3fn, contiguous
+    indices: torch.Tensor,      # [seq_q, kv_groups, topk] or [seq_q, topk] int32; -1 = masked
+    sm_scale: float,
+    return_lse: bool = False,
+    block_n: int = 16,          # accepted for API compatibility; tiles are fixed per kernel
+    block_h: int = 16,
+    num_stages: int = 2,
+    num_warps: int = 4,
+    *,
+    num_kv_splits: int | None = None,
+    workspace: torch.Tensor | None = None,
+):
+    """Sparse MLA decode reading fp8_ds_mla pages.
+
+    `indices` are FLAT SLOT indices into the paged cache (block * block_size +
+    offset).  Returns `out` [seq_q, h_q, 512] in q.dtype, plus the natural-log
+    `lse` [seq_q, h_q] fp32 when `return_lse` (-inf and a zero row for a query
+    that selected nothing).  `num_kv_splits`: None/0 = heuristic, 1 = single
+    pass, S > 1 = split the top-k axis S ways and merge by LSE.  The tuning
+    kwargs of the reference (block_n, block_h, num_stages, num_warps) do not
+    change the result and are ignored.
+    """
+    assert kv_cache.dtype in (torch.uint8, torch.float8_e4m3fn), kv_cache.dtype
+    assert kv_cache.is_contiguous(), "kv_cache must be contiguous"
+    assert q.stride(-1) == 1 and indices.stride(-1) == 1, "need unit last-dim strides"
+    assert q.dtype in (torch.bfloat16, torch.float32), (
+        f"rope is stored bf16; q must be bf16 (fp32 allowed for testing), got {q.dtype}"
+    )
+    kv_u8 = kv_cache.view(torch.uint8).reshape(-1, ROW_BYTES)
+    num_slots = kv_u8.shape[0]
+
+    seq_q, h_q, dim_qk = q.shape
+    assert dim_qk == NOPE + ROPE, f"expected {NOPE + ROPE}, got {dim_qk}"
+    if indices.dim() == 2:
+        indices = indices.unsqueeze(1)
+    kv_groups, topk = indices.shape[1], indices.shape[2]
+    assert h_q % kv_groups == 0, f"h_q={h_q} not divisible by kv_groups={kv_groups}"
+    assert indices.dtype == torch.int32, f"indices must be int32, got {indices.dtype}"
+    N.require_cuda(q, kv_u8, indices)
+
+    # the kernels read q in 16-byte vectors; re-lay a misaligned view once
+    vec = 8 if q.dtype == torch.bfloat16 else 4
+    if q.data_ptr() % 16 or q.stride(0) % vec or q.stride(1) % vec:
+        q = q.contiguous()
+        if q.data_ptr() % 16:
+            q = q.clone()
+
+    out = torch.empty((seq_q, h_q, NOPE), dtype=q.dtype, device=q.device)
+    lse = torch.empty((seq_q, h_q), dtype=torch.float32, device=q.device) if return_lse else None
+
+    splits = 0 if num_kv_splits is None else int(num_kv_splits)
+    need = decode_workspace_bytes(seq_q, h_q, kv_groups, topk, splits)
+    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_ptr = workspace.data_ptr() if (need and workspace is not None) else None
+    ws_bytes = workspace.numel() * workspace.element_size() if (need and workspace is not None) else 0
+
+    rc = N.lib().fp8mla_sparse_decode(
+        q.data_ptr(), N.DTYPE_BF16 if q.dtype == torch.bfloat16 else N.DTYPE_F32,
+        seq_q, h_q, q.stride(0), q.stride(1),
+        kv_u8.data_ptr(), num_slots,
+        indices.data_ptr(), kv_groups, topk, indices.stride(0), indices.stride(1),
+        float(sm_scale),
+        out.data_ptr(), out.stride(0), out.stride(1),
+        lse.data_ptr() if lse is not None else None, lse.stride(0) if lse is not None else 0,
+        splits, ws_ptr, ws_bytes, N.stream_ptr(q.device))
+    N.check(rc, "fp8_ds_mla_sparse_decode")
+    return (out, lse) if return_lse else out
