@@ -79,7 +79,9 @@ def test_writer_byte_exact_with_reference_golden(cuda_device):
 
 def test_writer_byte_exact_on_amax_spread_and_zero_tiles(cuda_device):
     """c4 edge (c): tile amax log-uniform in [1e-4, 1e4] plus exact-zero tiles."""
-    w = synthetic.make_host("c4", seed=2, B=1, pool_slots=8192)
+    s = synthetic.Shape("spread", B=1, H=16, topk=128, ctx=8192, pool_slots=8192,
+                        amax_spread=True)
+    w = synthetic.make_host(s, seed=2)
     U.device_pool(w.kv_src_bits, check_against_oracle=True)
 
 
