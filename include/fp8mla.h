@@ -58,6 +58,15 @@ FP8MLA_API const char* fp8mla_last_error(void);
 FP8MLA_API int fp8mla_abi_version(void);
 
 /*
+ * Device-side status word of the current device: 0, or the bits the decode
+ * kernels set when a bounded on-chip wait gave up (bit 0 = wait timeout,
+ * bits 8.. = which wait).  Synchronises `stream`; `reset` != 0 clears it.
+ * Returns FP8MLA_OK and stores the word in *status.  No reference
+ * counterpart (the reference's Triton kernels have no on-chip waits).
+ */
+FP8MLA_API int fp8mla_device_status(unsigned int* status, int reset, void* stream);
+
+/*
  * Split-KV count the decode picks when called with num_splits = 0.
  * Replaces the host heuristic `_choose_num_kv_splits`
  * (tests/fixtures/triton_mla_sparse_kernel_pr47629.py:406-423): a power of two

@@ -288,3 +288,25 @@ def test_cuda_graph_capture_replays_identically(cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(out, eager)
     del g
+
+
+def test_no_on_chip_wait_timed_out(cuda_device):
+    """Runs after the decode tests in this file: no bounded wait gave up."""
+    from vllm_fp8kv import _native as N
+
+    w = synthetic.make_host(synthetic.Shape("s", B=3, H=128, topk=200, ctx=2048, pool_slots=8192),
+                            seed=11)
+    pool = U.device_pool(w.kv_src_bits, check_against_oracle=False)
+    fp8_ds_mla_sparse_decode(U.bf16_tensor(w.q_bits), pool, torch.from_numpy(w.slots).cuda(),
+                             w.sm_scale)
+    assert N.device_status(reset=True) == 0
+
+
+def test_h128_bf16_dispatches_to_tcgen05(cuda_device):
+    from vllm_fp8kv.fp8_ds_mla_sparse_decode import decode_kernel_name
+
+    assert decode_kernel_name(64, 128, 1, 2048) == "decode_tc_kernel"
+    assert decode_kernel_name(64, 256, 2, 2048) == "decode_tc_kernel"
+    assert decode_kernel_name(64, 128, 1, 2048, torch.float32) == "decode_mma_kernel"
+    assert decode_kernel_name(256, 16, 1, 2048, torch.bfloat16, 8) == \
+        "decode_mma_kernel+merge_splits_kernel"

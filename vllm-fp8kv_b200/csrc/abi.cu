@@ -100,6 +100,14 @@ const char* fp8mla_last_error(void) { return g_last_error; }
 
 int fp8mla_abi_version(void) { return 1; }
 
+int fp8mla_device_status(unsigned int* status, int reset, void* stream) {
+  g_last_error[0] = 0;
+  if (status == nullptr) return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "status is NULL");
+  *status = 0;
+  if (int rc = require_sm100()) return rc;
+  return read_device_status(status, reset != 0, static_cast<cudaStream_t>(stream));
+}
+
 int fp8mla_choose_num_splits(int64_t T, int64_t H, int64_t G, int64_t topk, int sm_count) {
   if (G <= 0 || H <= 0 || H % G != 0) return 1;
   return pick_splits(T, H, G, topk, sm_count);

@@ -29,6 +29,8 @@ struct DecodeArgs {
 };
 
 int launch_decode_mma(const DecodeArgs& a, cudaStream_t st);
+int launch_merge_splits(const DecodeArgs& a, cudaStream_t st);
+int read_device_status(unsigned int* status, bool reset, cudaStream_t st);
 int launch_decode_tc(const DecodeArgs& a, cudaStream_t st);
 bool decode_tc_supported(const DecodeArgs& a);
 

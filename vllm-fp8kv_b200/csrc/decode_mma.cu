@@ -327,6 +327,10 @@ int launch_decode_mma(const DecodeArgs& a, cudaStream_t st) {
   else
     rc = go(decode_mma_kernel<float, float>);
   if (rc != FP8MLA_OK || a.num_splits == 1) return rc;
+  return launch_merge_splits(a, st);
+}
+
+int launch_merge_splits(const DecodeArgs& a, cudaStream_t st) {
   dim3 mgrid((unsigned)(a.T * a.H));
   if (a.q_dtype == FP8MLA_DTYPE_BF16)
     merge_splits_kernel<__nv_bfloat16><<<mgrid, 128, 0, st>>>(a);

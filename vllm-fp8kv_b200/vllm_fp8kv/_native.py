@@ -26,6 +26,7 @@ _P, _I64, _I32, _F32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_f
 SIGNATURES = {
     "fp8mla_last_error": (ctypes.c_char_p, []),
     "fp8mla_abi_version": (_I32, []),
+    "fp8mla_device_status": (_I32, [ctypes.POINTER(ctypes.c_uint), _I32, _P]),
     "fp8mla_choose_num_splits": (_I32, [_I64, _I64, _I64, _I64, _I32]),
     "fp8mla_decode_workspace_bytes": (_I64, [_I64, _I64, _I64, _I64, _I32]),
     "fp8mla_decode_kernel_name": (ctypes.c_char_p, [_I64, _I64, _I64, _I64, _I32, _I32]),
@@ -76,6 +77,14 @@ def check(rc: int, what: str) -> None:
     if rc == ERR_INVALID_ARGUMENT:
         raise AssertionError(f"{what}: {msg}")
     raise Fp8MlaError(f"{what} failed ({rc}): {msg}")
+
+
+def device_status(reset: bool = True, device=None) -> int:
+    """Device status word (0 = no bounded on-chip wait timed out); synchronises."""
+    v = ctypes.c_uint(0)
+    check(lib().fp8mla_device_status(ctypes.byref(v), int(reset), stream_ptr(device)),
+          "fp8mla_device_status")
+    return v.value
 
 
 def stream_ptr(device) -> int:
