@@ -131,6 +131,28 @@ FP8MLA_API int fp8mla_sparse_decode(const void* q, int q_dtype, int64_t T, int64
                          int64_t workspace_bytes, void* stream);
 
 /*
+ * fp8mla_sparse_decode for callers that cannot allocate device memory.
+ * No counterpart in the reference.  Same arguments and behaviour as
+ * fp8mla_sparse_decode minus the workspace: the split-KV scratch comes from a
+ * fixed 32 MiB array inside this library (held by each GPU that loads it until
+ * the process exits) instead of from the caller, and nothing is allocated.
+ * Shapes whose split workspace would exceed 32 MiB return
+ * FP8MLA_ERR_WORKSPACE.  The array's address is looked up on the first call
+ * made on each device, so make that call before any stream capture.  All
+ * calls on a device share the array: calls that can overlap on the GPU race
+ * and must be serialised by the caller.
+ */
+FP8MLA_API int fp8mla_sparse_decode_noalloc(const void* q, int q_dtype, int64_t T, int64_t H,
+                                            int64_t q_stride_t, int64_t q_stride_h,
+                                            const uint8_t* kv, int64_t num_slots,
+                                            const int32_t* indices, int64_t G, int64_t topk,
+                                            int64_t idx_stride_t, int64_t idx_stride_g,
+                                            float sm_scale,
+                                            void* out, int64_t out_stride_t, int64_t out_stride_h,
+                                            float* lse, int64_t lse_stride_t,
+                                            int num_splits, void* stream);
+
+/*
  * fp8_ds_mla cache writer: quantize bf16 latent + rope into 656-byte rows.
  *
  * Replaces vLLM's `concat_and_cache_mla(..., kv_cache_dtype="fp8_ds_mla")`

@@ -38,6 +38,9 @@ SIGNATURES = {
         _P, _I64, _I64,                        # out, out strides
         _P, _I64,                              # lse, lse stride
         _I32, _P, _I64, _P]),                  # num_splits, workspace, bytes, stream
+    "fp8mla_sparse_decode_noalloc": (_I32, [
+        _P, _I32, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _F32,
+        _P, _I64, _I64, _P, _I64, _I32, _P]),
     "fp8mla_ds_mla_write": (_I32, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P]),
     "fp8mla_dequant_e4m3": (_I32, [_P, _I64, _P, _I32, _I32, _P]),
     "fp8mla_convert_req_index": (_I32, [_P, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64,
