@@ -6,24 +6,34 @@
 //   O += P V    M=128 heads, N=256 output dims, K=32 tokens
 // A 128 x 512 fp32 O fills a whole SM's tensor memory, so each (token, group)
 // runs on two CTAs: CTA r accumulates O[:, 256r : 256r+256) and both compute
-// the full S (no cross-SM traffic).  Tensor-memory map (512 columns):
+// the full S (no cross-SM traffic; the second CTA's row reads hit L2).
+//
+// An MMA that accumulates into the tile the previous MMA wrote waits for it
+// (~190 cycles on B200, whatever N), so a single 36-step QK^T chain would leave
+// the tensor pipe idle most of the time.  Each tile's QK^T is therefore split
+// into 3 independent partial accumulators over disjoint 192-dim slices of
+// d=576, issued interleaved, and the previous tile's PV is slipped into the
+// same stream as soon as its P is ready; the softmax adds the 3 partials.
+//
+// Tensor-memory map (512 columns):
 //   [  0,256)  O (fp32)
-//   [256,320)  S/P double buffer: S fp32 32 cols; P bf16 packed in its first 16
-//   [320,512)  Q dims [0,384) as the A operand of the TMEM-A MMA (bf16x2)
-// Q dims [384,576) stay in shared memory (128B-swizzled, K-major).
+//   [256,448)  2 S buffers x 3 partials x 32 fp32 columns; P (bf16x2) is
+//              written over partial 0 of its buffer
+//   [448,512)  Q dims [0,128) as the A operand of the TMEM-A MMA (bf16x2)
+// Q dims [128,576) live in shared memory (7 x 64-dim 128B-swizzled blocks).
 //
 // Warp roles (416 threads):
 //   warps 0-3   softmax + epilogue: thread i owns head i = TMEM lane i, so the
 //               row max / sum / lazy rescale of its O row need no cross-thread
-//               reduction.  The running max is only raised when a tile exceeds
-//               it by more than 8 (log2 units); P <= 2^8 stays exact enough in
-//               bf16 and the final 1/l and LSE use the same reference max.
+//               reduction.  The reference max is only raised when a tile
+//               exceeds it by more than 8 (log2 units); P <= 2^8 keeps its
+//               bf16 precision and the final 1/l and LSE use the same max.
 //   warp 4      TMEM allocation and the single-thread MMA issuer
-//   warps 5-12  gather + dequant: each warp owns 4 of the 32 rows of a tile,
-//               issues their 41 x 16-byte cp.async (zero fill for masked slots,
-//               no global read), then writes bf16(e4m3 * scale) and the raw
-//               rope into a 128B-swizzled tile that is the K-major B operand of
-//               QK^T and, read MN-major, the V operand of PV.
+//   warps 5-12  gather + dequant: each warp owns 4 of the 32 rows of a tile and
+//               loads them straight into registers two tiles ahead (no load is
+//               issued for a masked slot), then writes bf16(e4m3 * scale) and
+//               the raw rope into a 128B-swizzled tile that is the K-major B
+//               operand of QK^T and, read MN-major, the V operand of PV.
 // Every mbarrier wait is bounded; a timeout sets g_device_status, the roles
 // drain what they issued and the CTA frees its tensor memory and returns.
 //
@@ -40,25 +50,25 @@ namespace tc {
 namespace {
 
 constexpr int kHeads = 128;
-constexpr int kN = 32;            // tokens per tile
-constexpr int kKStages = 3;       // dequantized tile stages
-constexpr int kRawStages = 3;     // raw row stages (gather ring)
-constexpr int kAhead = 2;         // raw tiles in flight ahead of dequant
-constexpr int kDv = 256;          // output dims per CTA
-constexpr int kQTmemDims = 384;   // q dims held in tensor memory
-constexpr int kQSmemBlocks = 3;   // q dims [384,576) as 3 x 64-dim swizzled blocks
-constexpr int kKBlocks = 9;       // 576 dims = 9 x 64-dim blocks
-constexpr int kKBlockBytes = kN * 128;            // 4096
+constexpr int kN = 32;             // tokens per tile
+constexpr int kChains = 3;         // independent partial-S accumulators per tile
+constexpr int kStepsPerChain = 12; // 36 k-steps / 3
+constexpr int kKStages = 3;        // dequantized tile stages
+constexpr int kDv = 256;           // output dims per CTA
+constexpr int kQTmemSteps = 8;     // k-steps 0..7 (q dims 0..127) read A from tensor memory
+constexpr int kQSmemBlocks = 7;    // q dims [128,576) as 7 x 64-dim swizzled blocks
+constexpr int kKBlocks = 9;        // 576 dims = 9 x 64-dim blocks
+constexpr int kKBlockBytes = kN * 128;                // 4096
 constexpr int kKTileBytes = kKBlocks * kKBlockBytes;  // 36864
-constexpr int kQBlockBytes = kHeads * 128;        // 16384
-constexpr int kRawTileBytes = kN * kRowBytes;     // 20992
+constexpr int kQBlockBytes = kHeads * 128;            // 16384
 constexpr int kSoftmaxWarps = 4;
 constexpr int kMmaWarp = 4;
 constexpr int kFirstLoadWarp = 5;
 constexpr int kLoadWarps = 8;
 constexpr int kThreads = (kSoftmaxWarps + 1 + kLoadWarps) * 32;  // 416
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 0, kColS = 256, kColQ = 320;
+constexpr uint32_t kColO = 0, kColS = 256, kColQ = 448;
+constexpr uint32_t kSBufCols = kChains * kN;  // 96
 constexpr float kRescaleThreshold = 8.0f;
 
 constexpr uint32_t kIdescQK = idesc_bf16(128, kN, false);
@@ -67,8 +77,7 @@ constexpr uint32_t kIdescPV = idesc_bf16(128, kDv, true);
 struct Smem {
   uint8_t q[kQSmemBlocks * kQBlockBytes];     // 1024-aligned (offset 0)
   uint8_t k[kKStages][kKTileBytes];           // 1024-aligned
-  uint8_t raw[kRawStages][kRawTileBytes];     // 16-aligned
-  uint8_t valid[kKStages][kN];
+  uint8_t vnib[kKStages][kLoadWarps];         // validity of 4 rows per load warp
   uint64_t kfull[kKStages], kempty[kKStages];
   uint64_t sfull[2], pfull[2], sfree[2];
   uint64_t qready, ofull, drain;
@@ -76,13 +85,21 @@ struct Smem {
 };
 static_assert(offsetof(Smem, k) % 1024 == 0, "swizzle atoms need 1024-B alignment");
 static_assert(kKTileBytes % 1024 == 0 && kQBlockBytes % 1024 == 0, "");
-static_assert(offsetof(Smem, raw) % 16 == 0, "");
 static_assert(offsetof(Smem, kfull) % 8 == 0, "");
+static_assert(sizeof(Smem) + 1024 <= 227 * 1024, "shared memory budget");
 
 // byte offset of the 16-byte chunk `c` (0..7) of row `r` in a 128B-swizzled block
 __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) {
   return r * 128u + ((c ^ (r & 7u)) << 4);
 }
+
+// One load-warp lane's share of a row: fp8 chunks p, p+8, p+16, p+24, rope chunk p,
+// and the row's 4 tile scales.
+struct RowPart {
+  uint4 f[4];
+  uint4 rope;
+  uint4 sc;
+};
 
 }  // namespace
 
@@ -140,14 +157,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
   if (warp < kSoftmaxWarps) {
     // ================================================= softmax + epilogue
     const int h = threadIdx.x;                       // head within the group = TMEM lane
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    const uint32_t trow = tmem + lane_off;
-    // ---- Q: dims [0,384) -> TMEM (A operand), dims [384,576) -> swizzled smem
+    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    // ---- Q: dims [0,128) -> TMEM (A operand), dims [128,576) -> swizzled smem
     {
       const uint4* qsrc = reinterpret_cast<const uint4*>(
           static_cast<const uint16_t*>(a.q) + t * a.q_st + (int64_t)(head0 + h) * a.q_sh);
-#pragma unroll 1
-      for (int c0 = 0; c0 < kQTmemDims / 2; c0 += 32) {   // 32 packed columns per store
+#pragma unroll
+      for (int c0 = 0; c0 < kQTmemSteps * 8; c0 += 32) {   // 32 packed columns per store
         uint32_t w[32];
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
@@ -164,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
 #pragma unroll
         for (int c = 0; c < 8; ++c)
           *reinterpret_cast<uint4*>(s.q + blk * kQBlockBytes + swz(h, c)) =
-              qsrc[(kQTmemDims / 8) + blk * 8 + c];
+              qsrc[kQTmemSteps * 2 + blk * 8 + c];
       tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
@@ -177,33 +193,34 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
       const int b = j & 1, ks = j % kKStages;
       ok = warp_wait(b_sfull + 8 * b, (j >> 1) & 1, 1);
       if (!ok) break;
-      ok = warp_wait(b_kfull + 8 * ks, (j / kKStages) & 1, 2);  // orders the valid flags
+      ok = warp_wait(b_kfull + 8 * ks, (j / kKStages) & 1, 2);  // orders the validity nibbles
       if (!ok) break;
       tc_fence_after();
-      uint32_t sr[32];
-      tmem_ld32(trow + kColS + 32 * b, sr);
-      uint32_t vmask;
-      {
-        const uint4 v0 = reinterpret_cast<const uint4*>(s.valid[ks])[0];
-        const uint4 v1 = reinterpret_cast<const uint4*>(s.valid[ks])[1];
-        const uint32_t vw[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        vmask = 0;
+      const uint32_t sb = trow + kColS + kSBufCols * b;
+      uint32_t s0[32], s1[32], s2[32];
+      tmem_ld32(sb, s0);
+      tmem_ld32(sb + kN, s1);
+      tmem_ld32(sb + 2 * kN, s2);
+      const uint2 nib = *reinterpret_cast<const uint2*>(s.vnib[ks]);
+      uint32_t vmask = 0;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) vmask |= ((vw[i >> 2] >> (8 * (i & 3))) & 1u) << i;
+      for (int w = 0; w < 4; ++w) {
+        vmask |= ((nib.x >> (8 * w)) & 0xFu) << (4 * w);
+        vmask |= ((nib.y >> (8 * w)) & 0xFu) << (16 + 4 * w);
       }
       tmem_wait_ld();
       float x[32];
       float tmax = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        x[i] = ((vmask >> i) & 1u) ? __uint_as_float(sr[i]) * a.scale_log2 : -INFINITY;
+        const float sv = __uint_as_float(s0[i]) + __uint_as_float(s1[i]) + __uint_as_float(s2[i]);
+        x[i] = ((vmask >> i) & 1u) ? sv * a.scale_log2 : -INFINITY;
         tmax = fmaxf(tmax, x[i]);
       }
       // lazy reference max: raise it only when this tile exceeds it by > threshold
       float alpha = 1.f;
-      bool raise = tmax > m_used + kRescaleThreshold || (m_used == -INFINITY && tmax > -INFINITY);
-      if (raise) {
-        alpha = (m_used == -INFINITY) ? 1.f : exp2f(m_used - tmax);
+      if (tmax > m_used + kRescaleThreshold || (m_used == -INFINITY && tmax > -INFINITY)) {
+        alpha = (m_used == -INFINITY) ? 1.f : ex2_approx(m_used - tmax);
         m_used = tmax;
         l *= alpha;
       }
@@ -227,11 +244,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
       uint32_t pk[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const float p0 = exp2f(x[2 * i] - mref), p1 = exp2f(x[2 * i + 1] - mref);
+        const float p0 = ex2_approx(x[2 * i] - mref), p1 = ex2_approx(x[2 * i + 1] - mref);
         l += p0 + p1;
         pk[i] = pack_bf16x2(p0, p1);
       }
-      tmem_st16(trow + kColS + 32 * b, pk);
+      tmem_st16(sb, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(b_pfull + 8 * b);
@@ -288,21 +305,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
     if (lane == 0) {
       bool ok = thread_wait(b_qready, 0, 5);
       tc_fence_after();
-      const uint32_t tS = tmem + kColS, tO = tmem + kColO, tQ = tmem + kColQ;
-      const uint32_t vbase = (uint32_t)half * 4u * kKBlockBytes;  // dims [256r, 256r+256)
+      const uint32_t tO = tmem + kColO, tQ = tmem + kColQ;
+      const uint64_t kdesc0 = sdesc_sw128(sk0, 16, 1024);
+      const uint64_t qdesc0 = sdesc_sw128(sq, 16, 1024);
+      const uint64_t vdesc0 =
+          sdesc_sw128(sk0 + (uint32_t)half * 4u * kKBlockBytes, kKBlockBytes, 1024);
+      int pv_next = 0;  // first tile whose PV is not issued yet
       auto issue_pv = [&](int jj) {
         const int bb = jj & 1, kss = jj % kKStages;
-        ok = ok && thread_wait(b_pfull + 8 * bb, (jj >> 1) & 1, 6);
-        if (!ok) return;
         tc_fence_after();
-        const uint32_t vtile = sk0 + kss * kKTileBytes + vbase;
+        const uint32_t pa = tmem + kColS + kSBufCols * bb;
+        const uint64_t vd = vdesc0 + (uint64_t)((kss * kKTileBytes) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < kN / 16; ++kk) {
-          const uint64_t bdesc = sdesc_sw128(vtile + kk * 2048, kKBlockBytes, 1024);
-          mma_ts(tO, tS + 32 * bb + 8 * kk, bdesc, kIdescPV, (jj > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kN / 16; ++kk)
+          mma_ts(tO, pa + 8 * kk, vd + (uint64_t)((kk * 2048) >> 4), kIdescPV,
+                 (jj > 0 || kk > 0) ? 1u : 0u);
         mma_commit(b_sfree + 8 * bb);
         mma_commit(b_kempty + 8 * kss);
+        pv_next = jj + 1;
       };
       for (int j = 0; j < ntiles && ok; ++j) {
         const int b = j & 1, ks = j % kKStages;
@@ -310,25 +330,44 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
         if (ok && j >= 2) ok = thread_wait(b_sfree + 8 * b, ((j - 2) >> 1) & 1, 8);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t ktile = sk0 + ks * kKTileBytes;
-#pragma unroll 4
-        for (int kst = 0; kst < kDqk / 16; ++kst) {
-          const uint64_t bdesc =
-              sdesc_sw128(ktile + (kst >> 2) * kKBlockBytes + (kst & 3) * 32, 16, 1024);
-          if (kst < kQTmemDims / 16) {
-            mma_ts(tS + 32 * b, tQ + 8 * kst, bdesc, kIdescQK, kst > 0 ? 1u : 0u);
-          } else {
-            const int qk = kst - kQTmemDims / 16;
-            const uint64_t adesc =
-                sdesc_sw128(sq + (qk >> 2) * kQBlockBytes + (qk & 3) * 32, 16, 1024);
-            mma_ss(tS + 32 * b, adesc, bdesc, kIdescQK, 1u);
+        const uint32_t tS = tmem + kColS + kSBufCols * b;
+        const uint64_t kd = kdesc0 + (uint64_t)((ks * kKTileBytes) >> 4);
+#pragma unroll
+        for (int i = 0; i < kStepsPerChain; ++i) {
+#pragma unroll
+          for (int c = 0; c < kChains; ++c) {
+            const int kst = c * kStepsPerChain + i;
+            const uint64_t bdesc =
+                kd + (uint64_t)((((kst >> 2) * kKBlockBytes) + (kst & 3) * 32) >> 4);
+            const uint32_t acc = i > 0 ? 1u : 0u;
+            if (kst < kQTmemSteps) {
+              mma_ts(tS + kN * c, tQ + 8 * kst, bdesc, kIdescQK, acc);
+            } else {
+              const int qs = kst - kQTmemSteps;
+              const uint64_t adesc =
+                  qdesc0 + (uint64_t)((((qs >> 2) * kQBlockBytes) + (qs & 3) * 32) >> 4);
+              mma_ss(tS + kN * c, adesc, bdesc, kIdescQK, acc);
+            }
           }
+          // slip the previous tile's PV in as soon as its P is ready
+          if ((i & 3) == 3 && pv_next == j - 1 &&
+              mbar_test(b_pfull + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1))
+            issue_pv(j - 1);
         }
         mma_commit(b_sfull + 8 * b);
-        if (j >= 1) issue_pv(j - 1);
+        if (pv_next == j - 1) {
+          ok = thread_wait(b_pfull + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1, 6);
+          if (!ok) break;
+          issue_pv(j - 1);
+        }
       }
-      if (ok && ntiles > 0) issue_pv(ntiles - 1);
-      if (ok && ntiles > 0) mma_commit(b_ofull);
+      if (ok && ntiles > 0) {
+        ok = thread_wait(b_pfull + 8 * ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, 6);
+        if (ok) {
+          issue_pv(ntiles - 1);
+          mma_commit(b_ofull);
+        }
+      }
       // drain: nothing this thread issued may still touch tensor memory
       mma_commit(b_drain);
       thread_wait(b_drain, 0, 9);
@@ -337,71 +376,70 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
   } else {
     // ================================================= gather + dequant
     const int lw = warp - kFirstLoadWarp;       // 0..7, owns rows 4lw..4lw+3 of each tile
-    const int r = lane & 3, p = lane >> 2;      // dequant mapping: row, 16-B part
+    const int r = lane & 3, p = lane >> 2;      // row within the 4, 16-byte part 0..7
     const int row = lw * 4 + r;
-    auto gather = [&](int jt) {
-      const int rs = jt % kRawStages;
+    auto load = [&](int jt, RowPart& P, bool& valid) {
+      const int pos = beg + jt * kN + row;
+      int64_t slot = -1;
+      if (pos < end) {
+        const int32_t v = idx_row[pos];
+        if (v >= 0 && (int64_t)v < a.num_slots) slot = v;
+      }
+      valid = slot >= 0;
+      if (valid) {
+        const uint8_t* src = a.kv + slot * (int64_t)kRowBytes;
 #pragma unroll
-      for (int rr = 0; rr < 4; ++rr) {
-        const int rw = lw * 4 + rr;
-        const int pos = beg + jt * kN + rw;
-        int64_t slot = -1;
-        if (pos < end) {
-          const int32_t v = idx_row[pos];
-          if (v >= 0 && (int64_t)v < a.num_slots) slot = v;
-        }
-        const bool okr = slot >= 0;
-        const uint8_t* src = a.kv + (okr ? slot : 0) * (int64_t)kRowBytes;
-        const uint32_t dst = smem_u32(s.raw[rs] + rw * kRowBytes);
-        cp_async16(dst + lane * 16, src + lane * 16, okr ? 16 : 0);
-        if (lane < kRowChunks16 - 32)
-          cp_async16(dst + (32 + lane) * 16, src + (32 + lane) * 16, okr ? 16 : 0);
+        for (int i = 0; i < 4; ++i) P.f[i] = ldg_nc_v4(src + (p + 8 * i) * 16);
+        P.rope = ldg_nc_v4(src + kRopeOff + 16 * p);
+        P.sc = ldg_nc_v4(src + kScaleOff);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) P.f[i] = make_uint4(0, 0, 0, 0);
+        P.rope = make_uint4(0, 0, 0, 0);
+        P.sc = make_uint4(0, 0, 0, 0);
       }
     };
-    for (int jt = 0; jt < kAhead; ++jt) {
-      if (jt < ntiles) gather(jt);
-      cp_async_commit();
-    }
     bool ok = true;
-    for (int j = 0; j < ntiles && ok; ++j) {
-      const int ks = j % kKStages, rs = j % kRawStages;
-      if (j + kAhead < ntiles) gather(j + kAhead);
-      cp_async_commit();
-      cp_async_wait<kAhead>();
-      __syncwarp();
+    auto step = [&](int j, const RowPart& cur, bool vcur, RowPart& nxt2, bool& vnxt2) {
+      if (!ok || j >= ntiles) return;
+      if (j + 2 < ntiles) load(j + 2, nxt2, vnxt2);
+      const int ks = j % kKStages;
       if (j >= kKStages) ok = warp_wait(b_kempty + 8 * ks, ((j / kKStages) + 1) & 1, 10);
-      if (!ok) break;
-      const uint8_t* rawrow = s.raw[rs] + row * kRowBytes;
+      if (!ok) return;
       uint8_t* ktile = s.k[ks];
+      const float scl[4] = {__uint_as_float(cur.sc.x), __uint_as_float(cur.sc.y),
+                            __uint_as_float(cur.sc.z), __uint_as_float(cur.sc.w)};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int c8 = p + 8 * i;                                   // fp8 16-byte chunk
-        const uint4 wv = *reinterpret_cast<const uint4*>(rawrow + c8 * 16);
-        const float sc = *reinterpret_cast<const float*>(rawrow + kScaleOff + 4 * i);
+        const int c8 = p + 8 * i;                  // fp8 16-byte chunk = dims 16*c8 .. +15
         float sx;
         bool fused;
-        prep_scale(sc, sx, fused);
+        prep_scale(scl[i], sx, fused);
         uint4 o0, o1;
-        dequant4_bf16(wv.x, sx, fused, o0.x, o0.y);
-        dequant4_bf16(wv.y, sx, fused, o0.z, o0.w);
-        dequant4_bf16(wv.z, sx, fused, o1.x, o1.y);
-        dequant4_bf16(wv.w, sx, fused, o1.z, o1.w);
+        dequant4_bf16(cur.f[i].x, sx, fused, o0.x, o0.y);
+        dequant4_bf16(cur.f[i].y, sx, fused, o0.z, o0.w);
+        dequant4_bf16(cur.f[i].z, sx, fused, o1.x, o1.y);
+        dequant4_bf16(cur.f[i].w, sx, fused, o1.z, o1.w);
         uint8_t* blk = ktile + (c8 >> 2) * kKBlockBytes;
         const uint32_t c0 = (uint32_t)(c8 & 3) * 2u;
         *reinterpret_cast<uint4*>(blk + swz(row, c0)) = o0;
         *reinterpret_cast<uint4*>(blk + swz(row, c0 + 1)) = o1;
       }
-      *reinterpret_cast<uint4*>(ktile + 8 * kKBlockBytes + swz(row, p)) =
-          *reinterpret_cast<const uint4*>(rawrow + kRopeOff + 16 * p);
-      if (p == 0) {
-        const int pos = beg + j * kN + row;
-        const int32_t v = pos < end ? idx_row[pos] : -1;
-        s.valid[ks][row] = (v >= 0 && (int64_t)v < a.num_slots) ? 1 : 0;
-      }
+      *reinterpret_cast<uint4*>(ktile + 8 * kKBlockBytes + swz(row, p)) = cur.rope;
+      const uint32_t vb = __ballot_sync(0xFFFFFFFFu, p == 0 && vcur);  // bits 0..3 = rows 4lw..+3
+      if (lane == 0) s.vnib[ks][lw] = (uint8_t)(vb & 0xFu);
       fence_proxy_async_smem();
       mbar_arrive(b_kfull + 8 * ks);
+    };
+    RowPart A, B, C;
+    bool vA = false, vB = false, vC = false;
+    if (ntiles > 0) load(0, A, vA);
+    if (ntiles > 1) load(1, B, vB);
+    for (int j = 0; j < ntiles && ok; j += 3) {
+      step(j, A, vA, C, vC);
+      step(j + 1, B, vB, A, vA);
+      step(j + 2, C, vC, B, vB);
     }
-    cp_async_wait<0>();
   }
 
   tc_fence_before();
