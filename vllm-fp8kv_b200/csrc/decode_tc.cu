@@ -2,25 +2,34 @@
 //
 // All 128 heads of a kv group share the gathered latent rows, so the heads
 // are the MMA M dimension (M = 128, one tcgen05 M-tile):
-//   S = Q K^T   M=128 heads, N=32 tokens, K=576 (36 k-steps of 16)
-//   O += P V    M=128 heads, N=256 output dims, K=32 tokens
+//   S = Q K^T   M=128 heads, N=64 tokens, K=576 (36 k-steps of 16)
+//   O += P V    M=128 heads, N=256 output dims, K=64 tokens (4 k-steps)
 // A 128 x 512 fp32 O fills a whole SM's tensor memory, so each (token, group)
-// runs on two CTAs: CTA r accumulates O[:, 256r : 256r+256) and both compute
+// runs on two CTAs: CTA h accumulates O[:, 256h : 256h+256) and both compute
 // the full S (no cross-SM traffic; the second CTA's row reads hit L2).
 //
-// An MMA that accumulates into the tile the previous MMA wrote waits for it
-// (~190 cycles on B200, whatever N), so a single 36-step QK^T chain would leave
-// the tensor pipe idle most of the time.  Each tile's QK^T is therefore split
-// into 3 independent partial accumulators over disjoint 192-dim slices of
-// d=576, issued interleaved, and the previous tile's PV is slipped into the
-// same stream as soon as its P is ready; the softmax adds the 3 partials.
+// Throughput model (B200, one SM): tcgen05.mma issued as straight-line code
+// runs back to back whatever the accumulator; an M=128 kind::f16 MMA costs
+// max(N/2 cycles of math, bytes read from shared memory / 128 B per cycle).
+// An N=32 QK^T step re-reads 4 KB of Q for 1 KB of K and runs at a third of
+// the math rate; N=64 with a third of Q held in tensor memory (TMEM-A MMA, no
+// shared-memory read for A) brings a 64-token tile to ~1.5K cycles of QK^T.
 //
 // Tensor-memory map (512 columns):
 //   [  0,256)  O (fp32)
-//   [256,448)  2 S buffers x 3 partials x 32 fp32 columns; P (bf16x2) is
-//              written over partial 0 of its buffer
-//   [448,512)  Q dims [0,128) as the A operand of the TMEM-A MMA (bf16x2)
-// Q dims [128,576) live in shared memory (7 x 64-dim 128B-swizzled blocks).
+//   [256,384)  2 S buffers x 64 fp32 columns; P (bf16x2, 32 columns) is
+//              written over the first half of its buffer
+//   [384,512)  Q dims [0,256) as the A operand of the TMEM-A MMA (bf16x2)
+// Shared memory (216 KB):
+//   q   Q dims [256,576): 5 x 64-dim 128B-swizzled blocks (128 rows)
+//   v   3-deep ring of this CTA's V blocks: tile dims [256h, 256h+256) as
+//       4 x 64-dim swizzled blocks of 64 rows -- the K-major B operand of
+//       QK^T and, read MN-major, the V operand of PV.  A slot is released
+//       when the tile's PV completes.
+//   nv  the tile's other 5 blocks (the other latent half and the rope),
+//       single-buffered: released as soon as the tile's QK^T completes.
+// QK^T issues the V-block k-steps first, so the loaders refill `nv` while
+// the pipe runs the previous tile's PV and this tile's first 16 k-steps.
 //
 // Warp roles (416 threads):
 //   warps 0-3   softmax + epilogue: thread i owns head i = TMEM lane i, so the
@@ -29,11 +38,12 @@
 //               exceeds it by more than 8 (log2 units); P <= 2^8 keeps its
 //               bf16 precision and the final 1/l and LSE use the same max.
 //   warp 4      TMEM allocation and the single-thread MMA issuer
-//   warps 5-12  gather + dequant: each warp owns 4 of the 32 rows of a tile and
-//               loads them straight into registers two tiles ahead (no load is
-//               issued for a masked slot), then writes bf16(e4m3 * scale) and
-//               the raw rope into a 128B-swizzled tile that is the K-major B
-//               operand of QK^T and, read MN-major, the V operand of PV.
+//   warps 5-12  gather + dequant: each warp owns 8 of the 64 rows of a tile
+//               (4 lanes per row) and loads them straight into registers one
+//               tile ahead, their slots two tiles ahead (no load is issued for
+//               a masked slot), then writes bf16(e4m3 * scale) and the raw rope
+//               into the swizzled blocks.
+// Pipe order per tile j: QK(j) [V blocks, then nv blocks], PV(j-1).
 // Every mbarrier wait is bounded; a timeout sets g_device_status, the roles
 // drain what they issued and the CTA frees its tensor memory and returns.
 //
@@ -50,42 +60,45 @@ namespace tc {
 namespace {
 
 constexpr int kHeads = 128;
-constexpr int kN = 32;             // tokens per tile
-constexpr int kChains = 3;         // independent partial-S accumulators per tile
-constexpr int kStepsPerChain = 12; // 36 k-steps / 3
-constexpr int kKStages = 3;        // dequantized tile stages
-constexpr int kDv = 256;           // output dims per CTA
-constexpr int kQTmemSteps = 8;     // k-steps 0..7 (q dims 0..127) read A from tensor memory
-constexpr int kQSmemBlocks = 7;    // q dims [128,576) as 7 x 64-dim swizzled blocks
-constexpr int kKBlocks = 9;        // 576 dims = 9 x 64-dim blocks
-constexpr int kKBlockBytes = kN * 128;                // 4096
-constexpr int kKTileBytes = kKBlocks * kKBlockBytes;  // 36864
-constexpr int kQBlockBytes = kHeads * 128;            // 16384
+constexpr int kN = 64;              // tokens per tile
+constexpr int kKSteps = 36;         // 576 / 16
+constexpr int kDv = 256;            // output dims per CTA
+constexpr int kQTmemSteps = 16;     // k-steps 0..15 (q dims 0..255) read A from tensor memory
+constexpr int kQSmemBlocks = 5;     // q dims [256,576) as 5 x 64-dim swizzled blocks
+constexpr int kBlkBytes = kN * 128;                 // 8192: one 64-dim block of a tile
+constexpr int kVBlocks = 4;                         // this CTA's latent half
+constexpr int kNvBlocks = 5;                        // other latent half + rope
+constexpr int kVSlotBytes = kVBlocks * kBlkBytes;   // 32768
+constexpr int kVStages = 3;
+constexpr int kQBlockBytes = kHeads * 128;          // 16384
 constexpr int kSoftmaxWarps = 4;
 constexpr int kMmaWarp = 4;
 constexpr int kFirstLoadWarp = 5;
 constexpr int kLoadWarps = 8;
+constexpr int kLoadThreads = kLoadWarps * 32;
 constexpr int kThreads = (kSoftmaxWarps + 1 + kLoadWarps) * 32;  // 416
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 0, kColS = 256, kColQ = 448;
-constexpr uint32_t kSBufCols = kChains * kN;  // 96
+constexpr uint32_t kColO = 0, kColS = 256, kColQ = 384;
+constexpr uint32_t kSBufCols = kN;  // 64
 constexpr float kRescaleThreshold = 8.0f;
 
 constexpr uint32_t kIdescQK = idesc_bf16(128, kN, false);
 constexpr uint32_t kIdescPV = idesc_bf16(128, kDv, true);
 
 struct Smem {
-  uint8_t q[kQSmemBlocks * kQBlockBytes];     // 1024-aligned (offset 0)
-  uint8_t k[kKStages][kKTileBytes];           // 1024-aligned
-  uint8_t vnib[kKStages][kLoadWarps];         // validity of 4 rows per load warp
-  uint64_t kfull[kKStages], kempty[kKStages];
+  uint8_t q[kQSmemBlocks * kQBlockBytes];   // 1024-aligned (offset 0)
+  uint8_t v[kVStages][kVSlotBytes];         // 1024-aligned
+  uint8_t nv[kNvBlocks * kBlkBytes];        // 1024-aligned
+  uint8_t vbits[kVStages][kLoadWarps];      // validity of the 8 rows of each load warp
+  uint64_t vfull[kVStages], vempty[kVStages];
+  uint64_t nvfull, nvempty;
   uint64_t sfull[2], pfull[2], sfree[2];
   uint64_t qready, ofull, drain;
   uint32_t tmem_base;
 };
-static_assert(offsetof(Smem, k) % 1024 == 0, "swizzle atoms need 1024-B alignment");
-static_assert(kKTileBytes % 1024 == 0 && kQBlockBytes % 1024 == 0, "");
-static_assert(offsetof(Smem, kfull) % 8 == 0, "");
+static_assert(offsetof(Smem, v) % 1024 == 0 && offsetof(Smem, nv) % 1024 == 0,
+              "swizzle atoms need 1024-B alignment");
+static_assert(offsetof(Smem, vfull) % 8 == 0, "");
 static_assert(sizeof(Smem) + 1024 <= 227 * 1024, "shared memory budget");
 
 // byte offset of the 16-byte chunk `c` (0..7) of row `r` in a 128B-swizzled block
@@ -93,13 +106,225 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) {
   return r * 128u + ((c ^ (r & 7u)) << 4);
 }
 
-// One load-warp lane's share of a row: fp8 chunks p, p+8, p+16, p+24, rope chunk p,
-// and the row's 4 tile scales.
+// Block `bi` (0..8) of a tile for CTA half H: V blocks live in the ring slot,
+// the rest in the nv buffer.
+template <int H>
+__host__ __device__ constexpr bool is_v_block(int bi) {
+  return bi >= 4 * H && bi < 4 * H + 4;
+}
+template <int H>
+__host__ __device__ constexpr int nv_index(int bi) {
+  return bi < 4 * H ? bi : bi - 4;
+}
+
+// Exact bf16(fp32(e4m3) * scale) of the 4 bytes of w: the hardware e4m3x2 ->
+// f16x2 conversion is exact (every e4m3 value, subnormals and NaN included, is
+// an f16), f16 -> f32 is exact, then one fp32 multiply and one RNE cast, as in
+// the reference (fp8_ds_mla_sparse_decode.py:152-164).
+__device__ __forceinline__ void dequant4_hw(uint32_t w, float s, uint32_t& lo, uint32_t& hi) {
+  uint32_t h01, h23;
+  asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n"
+      " cvt.rn.f16x2.e4m3x2 %0, l;\n cvt.rn.f16x2.e4m3x2 %1, h;\n}\n"
+      : "=r"(h01), "=r"(h23)
+      : "r"(w));
+  const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+  const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+  lo = pack_bf16x2(f01.x * s, f01.y * s);
+  hi = pack_bf16x2(f23.x * s, f23.y * s);
+}
+
+// One load-warp lane's share of a row: fp8 chunks p + 4i (i = 0..7, chunk i
+// lands in tile block i), rope chunks p and p + 4, and the row's 4 tile scales.
 struct RowPart {
-  uint4 f[4];
-  uint4 rope;
+  uint4 f[8];
+  uint4 rope[2];
   uint4 sc;
 };
+
+struct Ctx {
+  const DecodeArgs* a;
+  const int32_t* idx_row;
+  int beg, end, ntiles;
+  uint32_t tmem;
+  uint32_t sq, sv0, snv;
+  uint32_t b_vfull, b_vempty, b_nvfull, b_nvempty;
+  uint32_t b_sfull, b_pfull, b_sfree, b_qready, b_ofull, b_drain;
+};
+
+// ------------------------------------------------------------------ MMA issuer
+// QK^T k-steps of one tile whose B block is (PartV ? a V block : an nv block),
+// in ascending k order.  Everything is unrolled: straight-line tcgen05.mma.
+template <int H, bool PartV>
+__device__ __forceinline__ void issue_qk_part(uint32_t tS, uint32_t tQ, uint64_t qdesc0,
+                                              uint64_t vdesc, uint64_t nvdesc) {
+  
+  constexpr int kFirst = 16 * H;  // first k-step issued for the tile (its V blocks)
+#pragma unroll
+  for (int kst = 0; kst < kKSteps; ++kst) {
+    const int bi = kst >> 2;
+    if (is_v_block<H>(bi) != PartV) continue;
+    const uint32_t acc = kst == kFirst ? 0u : 1u;
+    const uint32_t boff = (PartV ? (bi - 4 * H) : nv_index<H>(bi)) * kBlkBytes + (kst & 3) * 32;
+    const uint64_t bdesc = (PartV ? vdesc : nvdesc) + (uint64_t)(boff >> 4);
+    if (kst < kQTmemSteps) {
+      mma_ts(tS, tQ + 8 * kst, bdesc, kIdescQK, acc);
+    } else {
+      const int qs = kst - kQTmemSteps;
+      const uint64_t adesc = qdesc0 + (uint64_t)(((qs >> 2) * kQBlockBytes + (qs & 3) * 32) >> 4);
+      mma_ss(tS, adesc, bdesc, kIdescQK, acc);
+    }
+  }
+}
+
+// Spin (without suspending) on an mbarrier phase the tensor pipe completes;
+// bounded like every other wait.
+__device__ __forceinline__ bool thread_spin(uint32_t bar, uint32_t parity, uint32_t where) {
+  for (uint32_t it = 0; it < (kMaxWaitIters << 4); ++it)
+    if (mbar_test(bar, parity)) return true;
+  atomicOr(&g_device_status, kStatusWaitTimeout | (where << 8));
+  return false;
+}
+
+template <int H>
+__device__ void mma_role(const Ctx& c) {
+  bool ok = thread_wait(c.b_qready, 0, 5);
+  tc_fence_after();
+  const uint32_t tO = c.tmem + kColO, tQ = c.tmem + kColQ;
+  const uint64_t qdesc0 = sdesc_sw128(c.sq, 16, 1024);
+  const uint64_t vdesc0 = sdesc_sw128(c.sv0, 16, 1024);
+  const uint64_t nvdesc = sdesc_sw128(c.snv, 16, 1024);
+  // V read MN-major: 64-dim blocks kBlkBytes apart (LBO), 8-token groups 1 KB apart (SBO)
+  const uint64_t pvdesc0 = sdesc_sw128(c.sv0, kBlkBytes, 1024);
+  auto issue_pv = [&](int jj) {
+    const int bb = jj & 1, vs = jj % kVStages;
+    tc_fence_after();
+    const uint32_t pa = c.tmem + kColS + kSBufCols * bb;
+    const uint64_t vd = pvdesc0 + (uint64_t)((vs * kVSlotBytes) >> 4);
+#pragma unroll
+    for (int kk = 0; kk < kN / 16; ++kk)
+      mma_ts(tO, pa + 8 * kk, vd + (uint64_t)((kk * 16 * 128) >> 4), kIdescPV,
+             (jj > 0 || kk > 0) ? 1u : 0u);
+    mma_commit(c.b_sfree + 8 * bb);
+    mma_commit(c.b_vempty + 8 * vs);
+  };
+  for (int j = 0; j < c.ntiles && ok; ++j) {
+    const int b = j & 1, vs = j % kVStages;
+    ok = thread_wait(c.b_vfull + 8 * vs, (j / kVStages) & 1, 7);
+    // S buffer b last held P(j-2): PV(j-2) must have finished reading it
+    if (ok && j >= 2) ok = thread_spin(c.b_sfree + 8 * b, ((j - 2) >> 1) & 1, 8);
+    if (!ok) break;
+    tc_fence_after();
+    const uint32_t tS = c.tmem + kColS + kSBufCols * b;
+    const uint64_t vdesc = vdesc0 + (uint64_t)((vs * kVSlotBytes) >> 4);
+    issue_qk_part<H, true>(tS, tQ, qdesc0, vdesc, nvdesc);
+    ok = thread_wait(c.b_nvfull, j & 1, 11);
+    if (!ok) break;
+    tc_fence_after();
+    issue_qk_part<H, false>(tS, tQ, qdesc0, vdesc, nvdesc);
+    mma_commit(c.b_sfull + 8 * b);
+    mma_commit(c.b_nvempty);
+    if (j >= 1) {
+      ok = thread_wait(c.b_pfull + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1, 6);
+      if (!ok) break;
+      issue_pv(j - 1);
+    }
+  }
+  if (ok && c.ntiles > 0) {
+    const int jl = c.ntiles - 1;
+    ok = thread_wait(c.b_pfull + 8 * (jl & 1), (jl >> 1) & 1, 6);
+    if (ok) {
+      issue_pv(jl);
+      mma_commit(c.b_ofull);
+    }
+  }
+  // drain: nothing this thread issued may still touch tensor memory
+  mma_commit(c.b_drain);
+  thread_wait(c.b_drain, 0, 9);
+}
+
+// ------------------------------------------------------------------ gather + dequant
+template <int H>
+__device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
+  const DecodeArgs& a = *c.a;
+  const int r = lane & 7, p = lane >> 3;  // row within the warp's 8, quarter 0..3
+  const int row = lw * 8 + r;
+  // the live slot of this lane's row of tile jt, or -1 (masked, out of range, past the end)
+  auto slot_of = [&](int jt) -> int32_t {
+    const int pos = c.beg + jt * kN + row;
+    if (pos >= c.end) return -1;
+    const int32_t v = c.idx_row[pos];
+    return (v >= 0 && (int64_t)v < a.num_slots) ? v : -1;
+  };
+  auto load = [&](int32_t slot, RowPart& P, bool& valid) {
+    valid = slot >= 0;
+    if (valid) {
+      const uint8_t* src = a.kv + slot * (int64_t)kRowBytes;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) P.f[i] = ldg_v4(src + (p + 4 * i) * 16);
+      P.rope[0] = ldg_v4(src + kRopeOff + 16 * p);
+      P.rope[1] = ldg_v4(src + kRopeOff + 16 * (p + 4));
+      P.sc = ldg_v4(src + kScaleOff);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) P.f[i] = make_uint4(0, 0, 0, 0);
+      P.rope[0] = P.rope[1] = make_uint4(0, 0, 0, 0);
+      P.sc = make_uint4(0, 0, 0, 0);
+    }
+  };
+  // dequantize chunk i (64-dim block i, 16 dims at 16p) of the row into `blk`
+  auto put = [&](const RowPart& P, int i, uint8_t* blk) {
+    const float sc = (i >> 1) == 0   ? __uint_as_float(P.sc.x)
+                     : (i >> 1) == 1 ? __uint_as_float(P.sc.y)
+                     : (i >> 1) == 2 ? __uint_as_float(P.sc.z)
+                                     : __uint_as_float(P.sc.w);
+    uint4 o0, o1;
+    dequant4_hw(P.f[i].x, sc, o0.x, o0.y);
+    dequant4_hw(P.f[i].y, sc, o0.z, o0.w);
+    dequant4_hw(P.f[i].z, sc, o1.x, o1.y);
+    dequant4_hw(P.f[i].w, sc, o1.z, o1.w);
+    *reinterpret_cast<uint4*>(blk + swz(row, 2 * p)) = o0;
+    *reinterpret_cast<uint4*>(blk + swz(row, 2 * p + 1)) = o1;
+  };
+  bool ok = true;
+  // slots are read one step before their rows: the index load's latency hides
+  // behind a tile of dequant instead of stalling the row loads
+  int32_t slot_next = c.ntiles > 1 ? slot_of(1) : -1;
+  auto step = [&](int j, const RowPart& cur, bool vcur, RowPart& nxt, bool& vnxt) {
+    if (!ok || j >= c.ntiles) return;
+    const int32_t slot1 = slot_next;
+    if (j + 2 < c.ntiles) slot_next = slot_of(j + 2);
+    if (j + 1 < c.ntiles) load(slot1, nxt, vnxt);
+    const int vs = j % kVStages;
+    // V blocks of tile j -> ring slot vs (free once PV(j-3) completed)
+    if (j >= kVStages) ok = warp_wait(c.b_vempty + 8 * vs, ((j / kVStages) + 1) & 1, 10);
+    if (!ok) return;
+    uint8_t* vslot = s.v[vs];
+#pragma unroll
+    for (int i = 4 * H; i < 4 * H + 4; ++i) put(cur, i, vslot + (i - 4 * H) * kBlkBytes);
+    const uint32_t vb = __ballot_sync(0xFFFFFFFFu, p == 0 && vcur);  // bits 0..7 = rows 8lw..+7
+    if (lane == 0) s.vbits[vs][lw] = (uint8_t)(vb & 0xFFu);
+    fence_proxy_async_smem();
+    mbar_arrive(c.b_vfull + 8 * vs);
+    // the other blocks -> nv (free once QK(j-1) completed)
+    if (j >= 1) ok = warp_wait(c.b_nvempty, (j - 1) & 1, 12);
+    if (!ok) return;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (!is_v_block<H>(i)) put(cur, i, s.nv + nv_index<H>(i) * kBlkBytes);
+    uint8_t* rope = s.nv + nv_index<H>(8) * kBlkBytes;
+    *reinterpret_cast<uint4*>(rope + swz(row, p)) = cur.rope[0];
+    *reinterpret_cast<uint4*>(rope + swz(row, p + 4)) = cur.rope[1];
+    fence_proxy_async_smem();
+    mbar_arrive(c.b_nvfull);
+  };
+  RowPart A, B;
+  bool vA = false, vB = false;
+  if (c.ntiles > 0) load(slot_of(0), A, vA);
+  for (int j = 0; j < c.ntiles && ok; j += 2) {
+    step(j, A, vA, B, vB);
+    step(j + 1, B, vB, A, vA);
+  }
+}
 
 }  // namespace
 
@@ -116,33 +341,43 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
   const int grp = (blockIdx.x % pairs_per_token) >> 1;
   const int half = blockIdx.x & 1;
   const int split = blockIdx.y;
-  const int beg = split * a.split_len;
-  const int end = min(a.topk, beg + a.split_len);
-  const int ntiles = end > beg ? (end - beg + kN - 1) / kN : 0;
-  const int32_t* idx_row = a.idx + t * a.idx_st + grp * a.idx_sg;
   const int head0 = grp * kHeads;
 
-  const uint32_t sq = smem_u32(s.q);
-  const uint32_t sk0 = smem_u32(s.k[0]);
-  const uint32_t b_kfull = smem_u32(&s.kfull[0]), b_kempty = smem_u32(&s.kempty[0]);
-  const uint32_t b_sfull = smem_u32(&s.sfull[0]), b_pfull = smem_u32(&s.pfull[0]);
-  const uint32_t b_sfree = smem_u32(&s.sfree[0]);
-  const uint32_t b_qready = smem_u32(&s.qready), b_ofull = smem_u32(&s.ofull);
-  const uint32_t b_drain = smem_u32(&s.drain);
+  Ctx c;
+  c.a = &a;
+  c.beg = split * a.split_len;
+  c.end = min(a.topk, c.beg + a.split_len);
+  c.ntiles = c.end > c.beg ? (c.end - c.beg + kN - 1) / kN : 0;
+  c.idx_row = a.idx + t * a.idx_st + grp * a.idx_sg;
+  c.sq = smem_u32(s.q);
+  c.sv0 = smem_u32(s.v[0]);
+  c.snv = smem_u32(s.nv);
+  c.b_vfull = smem_u32(&s.vfull[0]);
+  c.b_vempty = smem_u32(&s.vempty[0]);
+  c.b_nvfull = smem_u32(&s.nvfull);
+  c.b_nvempty = smem_u32(&s.nvempty);
+  c.b_sfull = smem_u32(&s.sfull[0]);
+  c.b_pfull = smem_u32(&s.pfull[0]);
+  c.b_sfree = smem_u32(&s.sfree[0]);
+  c.b_qready = smem_u32(&s.qready);
+  c.b_ofull = smem_u32(&s.ofull);
+  c.b_drain = smem_u32(&s.drain);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kKStages; ++i) {
-      mbar_init(b_kfull + 8 * i, kLoadWarps * 32);
-      mbar_init(b_kempty + 8 * i, 1);
+    for (int i = 0; i < kVStages; ++i) {
+      mbar_init(c.b_vfull + 8 * i, kLoadThreads);
+      mbar_init(c.b_vempty + 8 * i, 1);
     }
+    mbar_init(c.b_nvfull, kLoadThreads);
+    mbar_init(c.b_nvempty, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(b_sfull + 8 * i, 1);
-      mbar_init(b_pfull + 8 * i, kSoftmaxWarps * 32);
-      mbar_init(b_sfree + 8 * i, 1);
+      mbar_init(c.b_sfull + 8 * i, 1);
+      mbar_init(c.b_pfull + 8 * i, kSoftmaxWarps * 32);
+      mbar_init(c.b_sfree + 8 * i, 1);
     }
-    mbar_init(b_qready, kSoftmaxWarps * 32);
-    mbar_init(b_ofull, 1);
-    mbar_init(b_drain, 1);
+    mbar_init(c.b_qready, kSoftmaxWarps * 32);
+    mbar_init(c.b_ofull, 1);
+    mbar_init(c.b_drain, 1);
     mbar_init_fence();
   }
   if (warp == kMmaWarp) {
@@ -152,13 +387,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = s.tmem_base;
+  c.tmem = s.tmem_base;
+  const uint32_t tmem = c.tmem;
 
   if (warp < kSoftmaxWarps) {
     // ================================================= softmax + epilogue
     const int h = threadIdx.x;                       // head within the group = TMEM lane
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-    // ---- Q: dims [0,128) -> TMEM (A operand), dims [128,576) -> swizzled smem
+    // ---- Q: dims [0,256) -> TMEM (A operand), dims [256,576) -> swizzled smem
     {
       const uint4* qsrc = reinterpret_cast<const uint4*>(
           static_cast<const uint16_t*>(a.q) + t * a.q_st + (int64_t)(head0 + h) * a.q_sh);
@@ -178,44 +414,37 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
 #pragma unroll
       for (int blk = 0; blk < kQSmemBlocks; ++blk)
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(s.q + blk * kQBlockBytes + swz(h, c)) =
-              qsrc[kQTmemSteps * 2 + blk * 8 + c];
+        for (int cc = 0; cc < 8; ++cc)
+          *reinterpret_cast<uint4*>(s.q + blk * kQBlockBytes + swz(h, cc)) =
+              qsrc[kQTmemSteps * 2 + blk * 8 + cc];
       tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(b_qready);
+      mbar_arrive(c.b_qready);
     }
 
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < ntiles && ok; ++j) {
-      const int b = j & 1, ks = j % kKStages;
-      ok = warp_wait(b_sfull + 8 * b, (j >> 1) & 1, 1);
+    for (int j = 0; j < c.ntiles && ok; ++j) {
+      const int b = j & 1, vs = j % kVStages;
+      ok = warp_wait(c.b_sfull + 8 * b, (j >> 1) & 1, 1);
       if (!ok) break;
-      ok = warp_wait(b_kfull + 8 * ks, (j / kKStages) & 1, 2);  // orders the validity nibbles
+      ok = warp_wait(c.b_vfull + 8 * vs, (j / kVStages) & 1, 2);  // orders the validity bits
       if (!ok) break;
       tc_fence_after();
       const uint32_t sb = trow + kColS + kSBufCols * b;
-      uint32_t s0[32], s1[32], s2[32];
+      uint32_t s0[32], s1[32];
       tmem_ld32(sb, s0);
-      tmem_ld32(sb + kN, s1);
-      tmem_ld32(sb + 2 * kN, s2);
-      const uint2 nib = *reinterpret_cast<const uint2*>(s.vnib[ks]);
-      uint32_t vmask = 0;
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        vmask |= ((nib.x >> (8 * w)) & 0xFu) << (4 * w);
-        vmask |= ((nib.y >> (8 * w)) & 0xFu) << (16 + 4 * w);
-      }
+      tmem_ld32(sb + 32, s1);
+      const uint2 vbw = *reinterpret_cast<const uint2*>(s.vbits[vs]);  // bit k = token k
       tmem_wait_ld();
-      float x[32];
+      float x[64];
       float tmax = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float sv = __uint_as_float(s0[i]) + __uint_as_float(s1[i]) + __uint_as_float(s2[i]);
-        x[i] = ((vmask >> i) & 1u) ? sv * a.scale_log2 : -INFINITY;
-        tmax = fmaxf(tmax, x[i]);
+        x[i] = ((vbw.x >> i) & 1u) ? __uint_as_float(s0[i]) * a.scale_log2 : -INFINITY;
+        x[32 + i] = ((vbw.y >> i) & 1u) ? __uint_as_float(s1[i]) * a.scale_log2 : -INFINITY;
+        tmax = fmaxf(tmax, fmaxf(x[i], x[32 + i]));
       }
       // lazy reference max: raise it only when this tile exceeds it by > threshold
       float alpha = 1.f;
@@ -226,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
       }
       // O rows with alpha < 1 need rescaling once PV(j-1) has finished writing O
       if (__any_sync(0xFFFFFFFFu, alpha != 1.f) && j > 0) {
-        ok = warp_wait(b_sfree + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1, 3);
+        ok = warp_wait(c.b_sfree + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1, 3);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll 1
@@ -241,21 +470,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
       }
       // nothing valid yet: every x is -inf, use 0 so exp2(-inf - ref) is 0, not NaN
       const float mref = (m_used == -INFINITY) ? 0.f : m_used;
-      uint32_t pk[16];
+      uint32_t pk[32];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < 32; ++i) {
         const float p0 = ex2_approx(x[2 * i] - mref), p1 = ex2_approx(x[2 * i + 1] - mref);
         l += p0 + p1;
         pk[i] = pack_bf16x2(p0, p1);
       }
-      tmem_st16(sb, pk);
+      tmem_st32(sb, pk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(b_pfull + 8 * b);
+      mbar_arrive(c.b_pfull + 8 * b);
     }
 
     // ---- epilogue
-    const bool have_o = ok && ntiles > 0 && warp_wait(b_ofull, 0, 4);
+    const bool have_o = ok && c.ntiles > 0 && warp_wait(c.b_ofull, 0, 4);
     if (have_o) tc_fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
     const float lse_v = l > 0.f ? m_used * kLn2 + logf(l) : -INFINITY;
@@ -303,143 +532,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
   } else if (warp == kMmaWarp) {
     // ================================================= MMA issuer
     if (lane == 0) {
-      bool ok = thread_wait(b_qready, 0, 5);
-      tc_fence_after();
-      const uint32_t tO = tmem + kColO, tQ = tmem + kColQ;
-      const uint64_t kdesc0 = sdesc_sw128(sk0, 16, 1024);
-      const uint64_t qdesc0 = sdesc_sw128(sq, 16, 1024);
-      const uint64_t vdesc0 =
-          sdesc_sw128(sk0 + (uint32_t)half * 4u * kKBlockBytes, kKBlockBytes, 1024);
-      int pv_next = 0;  // first tile whose PV is not issued yet
-      auto issue_pv = [&](int jj) {
-        const int bb = jj & 1, kss = jj % kKStages;
-        tc_fence_after();
-        const uint32_t pa = tmem + kColS + kSBufCols * bb;
-        const uint64_t vd = vdesc0 + (uint64_t)((kss * kKTileBytes) >> 4);
-#pragma unroll
-        for (int kk = 0; kk < kN / 16; ++kk)
-          mma_ts(tO, pa + 8 * kk, vd + (uint64_t)((kk * 2048) >> 4), kIdescPV,
-                 (jj > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(b_sfree + 8 * bb);
-        mma_commit(b_kempty + 8 * kss);
-        pv_next = jj + 1;
-      };
-      for (int j = 0; j < ntiles && ok; ++j) {
-        const int b = j & 1, ks = j % kKStages;
-        ok = thread_wait(b_kfull + 8 * ks, (j / kKStages) & 1, 7);
-        if (ok && j >= 2) ok = thread_wait(b_sfree + 8 * b, ((j - 2) >> 1) & 1, 8);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t tS = tmem + kColS + kSBufCols * b;
-        const uint64_t kd = kdesc0 + (uint64_t)((ks * kKTileBytes) >> 4);
-#pragma unroll
-        for (int i = 0; i < kStepsPerChain; ++i) {
-#pragma unroll
-          for (int c = 0; c < kChains; ++c) {
-            const int kst = c * kStepsPerChain + i;
-            const uint64_t bdesc =
-                kd + (uint64_t)((((kst >> 2) * kKBlockBytes) + (kst & 3) * 32) >> 4);
-            const uint32_t acc = i > 0 ? 1u : 0u;
-            if (kst < kQTmemSteps) {
-              mma_ts(tS + kN * c, tQ + 8 * kst, bdesc, kIdescQK, acc);
-            } else {
-              const int qs = kst - kQTmemSteps;
-              const uint64_t adesc =
-                  qdesc0 + (uint64_t)((((qs >> 2) * kQBlockBytes) + (qs & 3) * 32) >> 4);
-              mma_ss(tS + kN * c, adesc, bdesc, kIdescQK, acc);
-            }
-          }
-          // slip the previous tile's PV in as soon as its P is ready
-          if ((i & 3) == 3 && pv_next == j - 1 &&
-              mbar_test(b_pfull + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1))
-            issue_pv(j - 1);
-        }
-        mma_commit(b_sfull + 8 * b);
-        if (pv_next == j - 1) {
-          ok = thread_wait(b_pfull + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1, 6);
-          if (!ok) break;
-          issue_pv(j - 1);
-        }
-      }
-      if (ok && ntiles > 0) {
-        ok = thread_wait(b_pfull + 8 * ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, 6);
-        if (ok) {
-          issue_pv(ntiles - 1);
-          mma_commit(b_ofull);
-        }
-      }
-      // drain: nothing this thread issued may still touch tensor memory
-      mma_commit(b_drain);
-      thread_wait(b_drain, 0, 9);
+      if (half == 0)
+        mma_role<0>(c);
+      else
+        mma_role<1>(c);
     }
     __syncwarp();
   } else {
     // ================================================= gather + dequant
-    const int lw = warp - kFirstLoadWarp;       // 0..7, owns rows 4lw..4lw+3 of each tile
-    const int r = lane & 3, p = lane >> 2;      // row within the 4, 16-byte part 0..7
-    const int row = lw * 4 + r;
-    auto load = [&](int jt, RowPart& P, bool& valid) {
-      const int pos = beg + jt * kN + row;
-      int64_t slot = -1;
-      if (pos < end) {
-        const int32_t v = idx_row[pos];
-        if (v >= 0 && (int64_t)v < a.num_slots) slot = v;
-      }
-      valid = slot >= 0;
-      if (valid) {
-        const uint8_t* src = a.kv + slot * (int64_t)kRowBytes;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) P.f[i] = ldg_nc_v4(src + (p + 8 * i) * 16);
-        P.rope = ldg_nc_v4(src + kRopeOff + 16 * p);
-        P.sc = ldg_nc_v4(src + kScaleOff);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) P.f[i] = make_uint4(0, 0, 0, 0);
-        P.rope = make_uint4(0, 0, 0, 0);
-        P.sc = make_uint4(0, 0, 0, 0);
-      }
-    };
-    bool ok = true;
-    auto step = [&](int j, const RowPart& cur, bool vcur, RowPart& nxt2, bool& vnxt2) {
-      if (!ok || j >= ntiles) return;
-      if (j + 2 < ntiles) load(j + 2, nxt2, vnxt2);
-      const int ks = j % kKStages;
-      if (j >= kKStages) ok = warp_wait(b_kempty + 8 * ks, ((j / kKStages) + 1) & 1, 10);
-      if (!ok) return;
-      uint8_t* ktile = s.k[ks];
-      const float scl[4] = {__uint_as_float(cur.sc.x), __uint_as_float(cur.sc.y),
-                            __uint_as_float(cur.sc.z), __uint_as_float(cur.sc.w)};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int c8 = p + 8 * i;                  // fp8 16-byte chunk = dims 16*c8 .. +15
-        float sx;
-        bool fused;
-        prep_scale(scl[i], sx, fused);
-        uint4 o0, o1;
-        dequant4_bf16(cur.f[i].x, sx, fused, o0.x, o0.y);
-        dequant4_bf16(cur.f[i].y, sx, fused, o0.z, o0.w);
-        dequant4_bf16(cur.f[i].z, sx, fused, o1.x, o1.y);
-        dequant4_bf16(cur.f[i].w, sx, fused, o1.z, o1.w);
-        uint8_t* blk = ktile + (c8 >> 2) * kKBlockBytes;
-        const uint32_t c0 = (uint32_t)(c8 & 3) * 2u;
-        *reinterpret_cast<uint4*>(blk + swz(row, c0)) = o0;
-        *reinterpret_cast<uint4*>(blk + swz(row, c0 + 1)) = o1;
-      }
-      *reinterpret_cast<uint4*>(ktile + 8 * kKBlockBytes + swz(row, p)) = cur.rope;
-      const uint32_t vb = __ballot_sync(0xFFFFFFFFu, p == 0 && vcur);  // bits 0..3 = rows 4lw..+3
-      if (lane == 0) s.vnib[ks][lw] = (uint8_t)(vb & 0xFu);
-      fence_proxy_async_smem();
-      mbar_arrive(b_kfull + 8 * ks);
-    };
-    RowPart A, B, C;
-    bool vA = false, vB = false, vC = false;
-    if (ntiles > 0) load(0, A, vA);
-    if (ntiles > 1) load(1, B, vB);
-    for (int j = 0; j < ntiles && ok; j += 3) {
-      step(j, A, vA, C, vC);
-      step(j + 1, B, vB, A, vA);
-      step(j + 2, C, vC, B, vB);
-    }
+    const int lw = warp - kFirstLoadWarp;  // 0..7
+    if (half == 0)
+      load_role<0>(c, s, lw, lane);
+    else
+      load_role<1>(c, s, lw, lane);
   }
 
   tc_fence_before();

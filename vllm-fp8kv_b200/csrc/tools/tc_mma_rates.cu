@@ -17,6 +17,7 @@ struct __align__(1024) SmemB {
 
 __global__ void __launch_bounds__(128, 1) mma_bench(int N, int chains, int ts, int iters,
                                                     long long* out_clk) {
+  // out_clk[0] = SM cycles, out_clk[1] = nanoseconds (globaltimer) for the same interval
   extern __shared__ __align__(1024) uint8_t sm[];
   const uint32_t base = smem_u32(sm);
   const uint32_t pad = ((base + 1023u) & ~1023u) - base;
@@ -42,17 +43,19 @@ __global__ void __launch_bounds__(128, 1) mma_bench(int N, int chains, int ts, i
       ad[k] = sdesc_sw128(sa + k * 32, 16, 1024);
       bd[k] = sdesc_sw128(sb + k * 32, 16, 1024);
     }
-    uint32_t dcol[4];
+    uint32_t dcol[8];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) dcol[c] = tmem + c * N;
+    for (int c = 0; c < 8; ++c) dcol[c] = tmem + c * N;
     const uint32_t acol = tmem + 448;
+    uint64_t g0, g1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g0));
     long long t0 = clock64();
     if (ts) {
       for (int it = 0; it < iters; ++it) {
 #pragma unroll
         for (int k = 0; k < 4; ++k)
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 8; ++c)
             if (c < chains) mma_ts(dcol[c], acol, bd[k], idesc, 1u);
       }
     } else {
@@ -60,14 +63,16 @@ __global__ void __launch_bounds__(128, 1) mma_bench(int N, int chains, int ts, i
 #pragma unroll
         for (int k = 0; k < 4; ++k)
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 8; ++c)
             if (c < chains) mma_ss(dcol[c], ad[k], bd[k], idesc, 1u);
       }
     }
     mma_commit(bar);
     bool ok = thread_wait(bar, 0, 1);
     long long t1 = clock64();
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g1));
     out_clk[0] = ok ? (t1 - t0) : -1;
+    out_clk[1] = (long long)(g1 - g0);
   }
   tc_fence_before();
   __syncthreads();
@@ -76,25 +81,27 @@ __global__ void __launch_bounds__(128, 1) mma_bench(int N, int chains, int ts, i
 
 int main() {
   long long* d_clk;
-  cudaMalloc(&d_clk, sizeof(long long));
+  cudaMalloc(&d_clk, 2 * sizeof(long long));
   const int smem = sizeof(SmemB) + 1024;
   cudaFuncSetAttribute(mma_bench, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int iters = 256;
-  printf("N chains ts | clk/MMA  MACs/clk (peak ~4096 per SM)\n");
-  int cfg[][2] = {{32, 1}, {32, 2}, {32, 4}, {64, 1}, {64, 2}, {64, 4}, {128, 1}, {128, 2},
-                  {256, 1}};
+  printf("N chains ts | clk/MMA  MACs/clk  ns/MMA  SM-MHz\n");
+  int cfg[][2] = {{32, 1}, {32, 2}, {32, 4}, {32, 6}, {32, 8}, {64, 1}, {64, 2}, {64, 4},
+                  {64, 6}, {128, 1}, {128, 2}, {128, 3}, {256, 1}};
   for (int ts = 0; ts < 2; ++ts)
     for (auto& c : cfg) {
       int N = c[0], ch = c[1];
       mma_bench<<<1, 128, smem>>>(N, ch, ts, 4, d_clk);  // warm
       mma_bench<<<1, 128, smem>>>(N, ch, ts, iters, d_clk);
       cudaError_t e = cudaDeviceSynchronize();
-      long long clk = 0;
-      cudaMemcpy(&clk, d_clk, sizeof(clk), cudaMemcpyDeviceToHost);
+      long long r[2] = {0, 0};
+      cudaMemcpy(r, d_clk, sizeof(r), cudaMemcpyDeviceToHost);
+      const long long clk = r[0];
       if (e != cudaSuccess) { printf("error %s\n", cudaGetErrorString(e)); return 1; }
       const double n_mma = (double)iters * 4 * ch;
       const double macs = n_mma * 128.0 * N * 16;
-      printf("%3d %d %d | %8.1f  %8.0f\n", N, ch, ts, clk / n_mma, macs / clk);
+      printf("%3d %d %d | %8.1f  %8.0f  %6.1f  %6.0f\n", N, ch, ts, clk / n_mma, macs / clk,
+             r[1] / n_mma, 1e3 * clk / (double)r[1]);
     }
   return 0;
 }
