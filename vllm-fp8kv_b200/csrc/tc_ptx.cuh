@@ -42,6 +42,12 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Arrive once and add `bytes` to the phase's expected transaction count.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
@@ -71,6 +77,7 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
 // Defined here: only decode_tc.cu includes this header (no relocatable device code).
 __device__ unsigned int g_device_status = 0;
 constexpr unsigned int kStatusWaitTimeout = 1u;
+constexpr unsigned int kStatusSmemAlign = 2u;
 // try_wait suspends for a hardware-chosen interval per call; 2^22 calls is
 // well beyond the longest legitimate wait of a CTA (its whole MMA chain, tens
 // of microseconds) yet ends a broken protocol within seconds.
