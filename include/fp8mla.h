@@ -60,9 +60,7 @@ FP8MLA_API int fp8mla_abi_version(void);
 /*
  * Device-side status word of the current device: 0, or the bits the decode
  * kernels set when a bounded on-chip wait gave up (bit 0 = wait timeout,
- * bits 8.. = which wait) or when the dynamic shared memory window was not
- * 1024-byte aligned (bit 1; the kernel then does no work).  Synchronises
- * `stream`; `reset` != 0 clears it.
+ * bits 8.. = which wait).  Synchronises `stream`; `reset` != 0 clears it.
  * Returns FP8MLA_OK and stores the word in *status.  No reference
  * counterpart (the reference's Triton kernels have no on-chip waits).
  */

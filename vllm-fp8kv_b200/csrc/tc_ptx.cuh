@@ -77,7 +77,6 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
 // Defined here: only decode_tc.cu includes this header (no relocatable device code).
 __device__ unsigned int g_device_status = 0;
 constexpr unsigned int kStatusWaitTimeout = 1u;
-constexpr unsigned int kStatusSmemAlign = 2u;
 // try_wait suspends for a hardware-chosen interval per call; 2^22 calls is
 // well beyond the longest legitimate wait of a CTA (its whole MMA chain, tens
 // of microseconds) yet ends a broken protocol within seconds.
