@@ -150,6 +150,25 @@ def test_c3_shape_h16_eight_splits(cuda_device):
     _shape_case("c3", B=8, pool_slots=1 << 18, splits=8)
 
 
+def test_c3_shape_large_grid_and_chunk_sizes_agree(cuda_device):
+    """A grid of at least two CTAs per SM takes the 32-token-chunk general
+    kernel (two CTAs share an SM); a small grid takes 64-token chunks.  Both
+    match the oracle, and the same requests decoded either way agree."""
+    w = synthetic.make_host("c3", seed=3, B=64, pool_slots=1 << 18)
+    pool = U.device_pool(w.kv_src_bits, check_against_oracle=False)
+    q = U.bf16_tensor(w.q_bits)
+    idx = torch.from_numpy(w.slots).cuda()
+    big, big_lse = _run(q, pool, idx, w.sm_scale, num_kv_splits=8)      # 512 CTAs
+    host_pool = pool.view(-1, 656).cpu().numpy()
+    qf = synthetic.bf16_to_f32(w.q_bits)
+    ref, ref_lse = O.sparse_decode(qf, host_pool, w.slots, w.sm_scale)
+    U.assert_close(big, ref)
+    U.assert_lse_close(big_lse, ref_lse)
+    small, small_lse = _run(q[:4], pool, idx[:4], w.sm_scale, num_kv_splits=8)  # 32 CTAs
+    U.assert_close(small, big[:4], max_abs=U.MAX_ABS_KERNEL_ROUNDING)
+    U.assert_lse_close(small_lse, big_lse[:4], max_abs=U.MAX_ABS_KERNEL_ROUNDING)
+
+
 def test_c4_shape_h64_edge_cases(cuda_device):
     """c4: tile amax log-uniform in [1e-4, 1e4] + zero tiles, leading 512
     indices of 8 requests masked.  Latents up to 1e4 make the scores ~1e4, so

@@ -154,6 +154,22 @@ __device__ __forceinline__ void dequant4_bf16(uint32_t w, float scale_x, bool fu
   hi = pack_bf16x2(f2, f3);
 }
 
+// Exact bf16(fp32(e4m3) * scale) of the 4 bytes of w: the hardware e4m3x2 ->
+// f16x2 conversion is exact (every e4m3 value, subnormals and NaN included, is
+// an f16), f16 -> f32 is exact, then one fp32 multiply and one RNE cast, as in
+// the reference (fp8_ds_mla_sparse_decode.py:152-164).
+__device__ __forceinline__ void dequant4_hw(uint32_t w, float s, uint32_t& lo, uint32_t& hi) {
+  uint32_t h01, h23;
+  asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n"
+      " cvt.rn.f16x2.e4m3x2 %0, l;\n cvt.rn.f16x2.e4m3x2 %1, h;\n}\n"
+      : "=r"(h01), "=r"(h23)
+      : "r"(w));
+  const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+  const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+  lo = pack_bf16x2(f01.x * s, f01.y * s);
+  hi = pack_bf16x2(f23.x * s, f23.y * s);
+}
+
 // Tile scale preparation for dequant4_bf16.
 __device__ __forceinline__ void prep_scale(float s, float& scale_x, bool& fused) {
   float sx = s * 1.329227995784915872903807060280344576e36f;  // * 2^120

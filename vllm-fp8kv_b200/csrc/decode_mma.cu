@@ -3,15 +3,22 @@
 // decode_tc.cu), plus the LSE merge of the split partials.
 //
 // One CTA = (query token, block of <= 16 heads, split of the top-k axis).
-// Per 64-token chunk:
-//   gather   4 threads per row issue 41 x 16-byte cp.async (zero-fill for
-//            masked slots: no global read), double-buffered;
-//   dequant  one warp per row: e4m3 * tile scale -> bf16 (bit-math, exact
-//            fp32 product then RNE, as the reference: decode.py:152-164);
-//   QK^T     8 warps x 8 tokens x 36 k-steps of m16n8k16 (d = 576);
-//   softmax  exp2 online softmax; a still -inf running max is replaced by 0
-//            so a fully masked chunk contributes nothing (decode.py:178-197);
-//   PV       8 warps x 64 output dims, V = the dequantized NoPE rows.
+// Two chunk sizes: with 32-token chunks two CTAs share an SM (~104 KB of
+// shared memory, <= 128 registers), so one CTA's gather latency hides behind
+// the other's math -- the choice when the grid has at least two CTAs per SM;
+// a grid of fewer CTAs takes 64-token chunks (one CTA per SM, half the
+// per-token synchronisation).  Per chunk:
+//   gather   256/BN threads per row issue the row's 41 x 16-byte cp.async
+//            (zero-fill for masked slots: no global read), double-buffered;
+//   dequant  one warp per row: e4m3 * tile scale -> bf16 (hardware e4m3x2 ->
+//            f16x2, exact fp32 product then RNE, as the reference:
+//            decode.py:152-164);
+//   QK^T     warp w: tokens 8(w % (BN/8))..+7 over a 1/(64/BN) share of
+//            d = 576 (m16n8k16 k-steps); the shares meet in shared memory;
+//   softmax  16 threads per head, BN/16 tokens each (exp2 form; a still -inf
+//            running max is replaced by 0 so a fully masked chunk contributes
+//            nothing: decode.py:178-197);
+//   PV       warp w: output dims 64w..+63, V = the dequantized NoPE rows.
 // Reference semantics: vllm_fp8kv/fp8_ds_mla_sparse_decode.py:77-211 and the
 // split/merge pair of tests/fixtures/triton_mla_sparse_kernel_pr47629.py:232-403.
 #include "common.cuh"
@@ -21,28 +28,42 @@ namespace fp8mla {
 
 namespace {
 
-constexpr int kBN = 64;         // tokens per chunk
 constexpr int kBH = 16;         // heads per CTA
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kKStride = 584;   // bf16 per sQ / sK row: 576 + 8 (1168 B = 73 x 16 B)
-constexpr int kPStride = kBN + 8;
 
+template <int BN>  // tokens per chunk: 32 or 64
+struct Cfg {
+  static constexpr int kParts = 64 / BN;              // d shares per token tile
+  static constexpr int kPartSteps = kDqk / 16 / kParts;  // k-steps per share
+  static constexpr int kPStride = BN + 8;
+  static constexpr int kSStride = BN + 1;
+  static constexpr int kRowThreads = kThreads / BN;   // gather threads per row
+  static constexpr int kMinBlocks = BN == 32 ? 2 : 1;
+  static_assert(kThreads / 32 == (BN / 8) * kParts, "one warp per (token tile, d share)");
+};
+
+template <int BN>
 struct Smem {
   uint16_t q[kBH * kKStride];
-  uint16_t k[kBN * kKStride];
-  uint8_t raw[2][kBN * kRowBytes];
-  uint16_t p[kBH * kPStride];
-  float red_max[kWarps][kBH];
-  float red_sum[kWarps][kBH];
-  int valid[2][kBN];
+  uint16_t k[BN * kKStride];
+  uint8_t raw[2][BN * kRowBytes];
+  uint16_t p[kBH * Cfg<BN>::kPStride];
+  float sp[Cfg<BN>::kParts][kBH * Cfg<BN>::kSStride];  // partial S per d share
+  float m_run[kBH], l_run[kBH], alpha[kBH];
+  int valid[2][BN];
 };
-static_assert(sizeof(Smem) <= 227 * 1024, "shared memory budget");
-static_assert(offsetof(Smem, raw) % 16 == 0, "cp.async destinations must be 16-B aligned");
+static_assert(2 * (sizeof(Smem<32>) + 1024) <= 228 * 1024, "two 32-token CTAs per SM");
+static_assert(sizeof(Smem<64>) <= 227 * 1024, "shared memory budget");
+static_assert(offsetof(Smem<32>, raw) % 16 == 0 && offsetof(Smem<64>, raw) % 16 == 0,
+              "cp.async destinations must be 16-B aligned");
 
-__device__ __forceinline__ void issue_gather(Smem& s, int buf, const DecodeArgs& a,
+template <int BN>
+__device__ __forceinline__ void issue_gather(Smem<BN>& s, int buf, const DecodeArgs& a,
                                              const int32_t* idx_row, int pos0, int end) {
-  const int r = threadIdx.x >> 2, sub = threadIdx.x & 3;
+  constexpr int kRT = Cfg<BN>::kRowThreads;
+  const int r = threadIdx.x / kRT, sub = threadIdx.x % kRT;
   const int pos = pos0 + r;
   int64_t slot = -1;
   if (pos < end) {
@@ -52,16 +73,19 @@ __device__ __forceinline__ void issue_gather(Smem& s, int buf, const DecodeArgs&
   const bool ok = slot >= 0;
   const uint8_t* src = a.kv + (ok ? slot : 0) * (int64_t)kRowBytes;
   const uint32_t dst = smem_u32(&s.raw[buf][r * kRowBytes]);
-  for (int j = sub; j < kRowChunks16; j += 4) cp_async16(dst + j * 16, src + j * 16, ok ? 16 : 0);
+  for (int j = sub; j < kRowChunks16; j += kRT) cp_async16(dst + j * 16, src + j * 16, ok ? 16 : 0);
   if (sub == 0) s.valid[buf][r] = ok;
 }
 
 }  // namespace
 
-template <typename QT, typename OT>
-__global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const DecodeArgs a) {
+template <typename QT, typename OT, int BN>
+__global__ void __launch_bounds__(kThreads, Cfg<BN>::kMinBlocks)
+    decode_mma_kernel(const DecodeArgs a) {
+  using C = Cfg<BN>;
+  constexpr int kBN = BN, kPStride = C::kPStride, kSStride = C::kSStride;
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  Smem& s = *reinterpret_cast<Smem*>(smem_raw);
+  Smem<BN>& s = *reinterpret_cast<Smem<BN>*>(smem_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
   const int nhb = a.G * a.hb_per_group;                    // head blocks per token
@@ -76,6 +100,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const DecodeArg
   const int beg = split * a.split_len;
   const int end = min(a.topk, beg + a.split_len);
   const int32_t* idx_row = a.idx + t * a.idx_st + grp * a.idx_sg;
+
+  const int nchunks = end > beg ? (end - beg + kBN - 1) / kBN : 0;
+  if (nchunks > 0) issue_gather(s, 0, a, idx_row, beg, end);
+  cp_async_commit();
+  if (nchunks > 1) issue_gather(s, 1, a, idx_row, beg + kBN, end);
+  cp_async_commit();
 
   // ---- Q -> smem (bf16), zero rows for padded heads
   for (int e = tid; e < kBH * (kDqk / 8); e += kThreads) {
@@ -94,16 +124,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const DecodeArg
     }
     *reinterpret_cast<uint4*>(&s.q[row * kKStride + c8 * 8]) = v;
   }
-
-  const int nchunks = end > beg ? (end - beg + kBN - 1) / kBN : 0;
-  if (nchunks > 0) issue_gather(s, 0, a, idx_row, beg, end);
-  cp_async_commit();
-  if (nchunks > 1) issue_gather(s, 1, a, idx_row, beg + kBN, end);
-  cp_async_commit();
+  if (tid < kBH) {
+    s.m_run[tid] = -INFINITY;
+    s.l_run[tid] = 0.f;
+  }
 
   const int g = lane >> 2, q4 = lane & 3;
-  float m_run[2] = {-INFINITY, -INFINITY};
-  float l_part[2] = {0.f, 0.f};
   float acc[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
@@ -111,29 +137,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const DecodeArg
   const uint32_t q_base = smem_u32(s.q);
   const uint32_t k_base = smem_u32(s.k);
   const uint32_t p_base = smem_u32(s.p);
+  // softmax ownership: head sh, tokens kTPT sp2 .. +kTPT-1 (16 threads per head)
+  constexpr int kTPT = kBN / 16;
+  const int sh = tid >> 4, sp2 = tid & 15;
 
   for (int c = 0; c < nchunks; ++c) {
     const int buf = c & 1;
     cp_async_wait<1>();
     __syncthreads();
-    // validity of this thread's two score columns, read before the gather of
-    // chunk c + 2 reuses the flag buffer
-    const int col = warp * 8 + q4 * 2;
-    const bool v0 = s.valid[buf][col] != 0, v1 = s.valid[buf][col + 1] != 0;
 
     // ---- dequant raw[buf] -> k (bf16): warp per row, lane owns 16 bytes
     for (int r = warp; r < kBN; r += kWarps) {
       const uint8_t* row = &s.raw[buf][r * kRowBytes];
       const uint4 w = reinterpret_cast<const uint4*>(row)[lane];
       const float sc = reinterpret_cast<const float*>(row + kScaleOff)[lane >> 3];
-      float sx;
-      bool fused;
-      prep_scale(sc, sx, fused);
       uint4 o0, o1;
-      dequant4_bf16(w.x, sx, fused, o0.x, o0.y);
-      dequant4_bf16(w.y, sx, fused, o0.z, o0.w);
-      dequant4_bf16(w.z, sx, fused, o1.x, o1.y);
-      dequant4_bf16(w.w, sx, fused, o1.z, o1.w);
+      dequant4_hw(w.x, sc, o0.x, o0.y);
+      dequant4_hw(w.y, sc, o0.z, o0.w);
+      dequant4_hw(w.z, sc, o1.x, o1.y);
+      dequant4_hw(w.w, sc, o1.z, o1.w);
       uint4* dst = reinterpret_cast<uint4*>(&s.k[r * kKStride + lane * 16]);
       dst[0] = o0;
       dst[1] = o1;
@@ -141,107 +163,107 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const DecodeArg
         reinterpret_cast<uint4*>(&s.k[r * kKStride + kNope])[lane] =
             reinterpret_cast<const uint4*>(row + kRopeOff)[lane];
     }
+    // validity of this thread's softmax tokens, read before the gather of
+    // chunk c + 2 reuses the flag buffer
+    bool vt[kTPT];
+#pragma unroll
+    for (int u = 0; u < kTPT; ++u) vt[u] = s.valid[buf][kTPT * sp2 + u] != 0;
     __syncthreads();
     if (c + 2 < nchunks) issue_gather(s, buf, a, idx_row, beg + (c + 2) * kBN, end);
     cp_async_commit();
 
-    // ---- S = Q K^T for this warp's 8 tokens
-    const int n0 = warp * 8;
-    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 6
-    for (int kk = 0; kk < kDqk / 16; kk += 2) {
-      uint32_t a0, a1, a2, a3, a4, a5, a6, a7, b0, b1, b2, b3;
-      const uint32_t qa = q_base + (((lane & 15) * kKStride + kk * 16 + (lane >> 4) * 8) << 1);
-      ldmatrix_x4(qa, a0, a1, a2, a3);
-      ldmatrix_x4(qa + 32, a4, a5, a6, a7);
-      const uint32_t kb = k_base + (((n0 + (lane & 7)) * kKStride + kk * 16 + (lane >> 3) * 8) << 1);
-      ldmatrix_x4(kb, b0, b1, b2, b3);
-      mma_bf16_16816(sacc, a0, a1, a2, a3, b0, b1);
-      mma_bf16_16816(sacc, a4, a5, a6, a7, b2, b3);
-    }
-
-    // ---- online softmax (exp2 form)
-    float x[4];
-    x[0] = (v0 && g < nh) ? sacc[0] * a.scale_log2 : -INFINITY;
-    x[1] = (v1 && g < nh) ? sacc[1] * a.scale_log2 : -INFINITY;
-    x[2] = (v0 && g + 8 < nh) ? sacc[2] * a.scale_log2 : -INFINITY;
-    x[3] = (v1 && g + 8 < nh) ? sacc[3] * a.scale_log2 : -INFINITY;
-    float mt0 = fmaxf(x[0], x[1]), mt1 = fmaxf(x[2], x[3]);
-#pragma unroll
-    for (int o = 1; o < 4; o <<= 1) {
-      mt0 = fmaxf(mt0, __shfl_xor_sync(0xFFFFFFFFu, mt0, o));
-      mt1 = fmaxf(mt1, __shfl_xor_sync(0xFFFFFFFFu, mt1, o));
-    }
-    if (q4 == 0) {
-      s.red_max[warp][g] = mt0;
-      s.red_max[warp][g + 8] = mt1;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      mt0 = fmaxf(mt0, s.red_max[w][g]);
-      mt1 = fmaxf(mt1, s.red_max[w][g + 8]);
-    }
-    float alpha[2], safe[2];
-    const float mn[2] = {fmaxf(m_run[0], mt0), fmaxf(m_run[1], mt1)};
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      safe[i] = (mn[i] == -INFINITY) ? 0.f : mn[i];
-      alpha[i] = exp2f(m_run[i] - safe[i]);
-      m_run[i] = mn[i];
-    }
-    const float p0 = exp2f(x[0] - safe[0]), p1 = exp2f(x[1] - safe[0]);
-    const float p2 = exp2f(x[2] - safe[1]), p3 = exp2f(x[3] - safe[1]);
-    l_part[0] = l_part[0] * alpha[0] + p0 + p1;
-    l_part[1] = l_part[1] * alpha[1] + p2 + p3;
-    *reinterpret_cast<uint32_t*>(&s.p[g * kPStride + col]) = pack_bf16x2(p0, p1);
-    *reinterpret_cast<uint32_t*>(&s.p[(g + 8) * kPStride + col]) = pack_bf16x2(p2, p3);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      acc[i][0] *= alpha[0];
-      acc[i][1] *= alpha[0];
-      acc[i][2] *= alpha[1];
-      acc[i][3] *= alpha[1];
+    // ---- partial S = Q K^T: tokens 8(w % (BN/8))..+7, d share w / (BN/8)
+    {
+      const int n0 = (warp % (kBN / 8)) * 8, k0 = (warp / (kBN / 8)) * C::kPartSteps;
+      float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 3
+      for (int kk = k0; kk < k0 + C::kPartSteps; kk += 2) {
+        uint32_t a0, a1, a2, a3, a4, a5, a6, a7, b0, b1, b2, b3;
+        const uint32_t qa = q_base + (((lane & 15) * kKStride + kk * 16 + (lane >> 4) * 8) << 1);
+        ldmatrix_x4(qa, a0, a1, a2, a3);
+        ldmatrix_x4(qa + 32, a4, a5, a6, a7);
+        const uint32_t kb = k_base + (((n0 + (lane & 7)) * kKStride + kk * 16 + (lane >> 3) * 8) << 1);
+        ldmatrix_x4(kb, b0, b1, b2, b3);
+        mma_bf16_16816(sacc, a0, a1, a2, a3, b0, b1);
+        mma_bf16_16816(sacc, a4, a5, a6, a7, b2, b3);
+      }
+      float* sp = s.sp[warp / (kBN / 8)];
+      const int col = n0 + q4 * 2;
+      sp[g * kSStride + col] = sacc[0];
+      sp[g * kSStride + col + 1] = sacc[1];
+      sp[(g + 8) * kSStride + col] = sacc[2];
+      sp[(g + 8) * kSStride + col + 1] = sacc[3];
     }
     __syncthreads();
 
-    // ---- O += P V for this warp's 64 output dims
-    const int d0 = warp * 64;
+    // ---- online softmax (exp2 form): 16 threads per head, kTPT tokens each
+    {
+      const int i0 = sh * kSStride + kTPT * sp2;
+      const bool hv = sh < nh;
+      float x[kTPT];
+      float mt = -INFINITY;
 #pragma unroll
-    for (int kk = 0; kk < kBN / 16; ++kk) {
-      uint32_t a0, a1, a2, a3;
-      ldmatrix_x4(p_base + (((lane & 15) * kPStride + kk * 16 + (lane >> 4) * 8) << 1), a0, a1, a2, a3);
+      for (int u = 0; u < kTPT; ++u) {
+        float sv = s.sp[0][i0 + u];
 #pragma unroll
-      for (int nt = 0; nt < 8; nt += 2) {
-        uint32_t b0, b1, b2, b3;
-        const int tok = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        ldmatrix_x4_trans(k_base + ((tok * kKStride + d0 + nt * 8 + (lane >> 4) * 8) << 1), b0, b1, b2, b3);
-        mma_bf16_16816(acc[nt], a0, a1, a2, a3, b0, b1);
-        mma_bf16_16816(acc[nt + 1], a0, a1, a2, a3, b2, b3);
+        for (int part = 1; part < C::kParts; ++part) sv += s.sp[part][i0 + u];
+        x[u] = (vt[u] && hv) ? sv * a.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, x[u]);
+      }
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xFFFFFFFFu, mt, o));
+      const float m_old = s.m_run[sh];
+      const float mn = fmaxf(m_old, mt);
+      const float safe = (mn == -INFINITY) ? 0.f : mn;
+      float ps = 0.f;
+#pragma unroll
+      for (int u = 0; u < kTPT; u += 2) {
+        const float p0 = exp2f(x[u] - safe), p1 = exp2f(x[u + 1] - safe);
+        *reinterpret_cast<uint32_t*>(&s.p[sh * kPStride + kTPT * sp2 + u]) = pack_bf16x2(p0, p1);
+        ps += p0 + p1;
+      }
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) ps += __shfl_xor_sync(0xFFFFFFFFu, ps, o);
+      if (sp2 == 0) {
+        const float al = exp2f(m_old - safe);
+        s.alpha[sh] = al;
+        s.l_run[sh] = s.l_run[sh] * al + ps;
+        s.m_run[sh] = mn;
+      }
+    }
+    __syncthreads();
+
+    // ---- O = alpha O + P V for this warp's 64 output dims
+    {
+      const float al0 = s.alpha[g], al1 = s.alpha[g + 8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        acc[i][0] *= al0;
+        acc[i][1] *= al0;
+        acc[i][2] *= al1;
+        acc[i][3] *= al1;
+      }
+      const int d0 = warp * 64;
+#pragma unroll
+      for (int kk = 0; kk < kBN / 16; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4(p_base + (((lane & 15) * kPStride + kk * 16 + (lane >> 4) * 8) << 1), a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < 8; nt += 2) {
+          uint32_t b0, b1, b2, b3;
+          const int tok = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          ldmatrix_x4_trans(k_base + ((tok * kKStride + d0 + nt * 8 + (lane >> 4) * 8) << 1), b0, b1, b2, b3);
+          mma_bf16_16816(acc[nt], a0, a1, a2, a3, b0, b1);
+          mma_bf16_16816(acc[nt + 1], a0, a1, a2, a3, b2, b3);
+        }
       }
     }
   }
   cp_async_wait<0>();
-
-  // ---- row sums across the quad and the 8 warps
-#pragma unroll
-  for (int o = 1; o < 4; o <<= 1) {
-    l_part[0] += __shfl_xor_sync(0xFFFFFFFFu, l_part[0], o);
-    l_part[1] += __shfl_xor_sync(0xFFFFFFFFu, l_part[1], o);
-  }
   __syncthreads();
-  if (q4 == 0) {
-    s.red_sum[warp][g] = l_part[0];
-    s.red_sum[warp][g + 8] = l_part[1];
-  }
-  __syncthreads();
-  float l[2] = {0.f, 0.f};
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
-    l[0] += s.red_sum[w][g];
-    l[1] += s.red_sum[w][g + 8];
-  }
 
+  const float l[2] = {s.l_run[g], s.l_run[g + 8]};
+  const float mr[2] = {s.m_run[g], s.m_run[g + 8]};
   const int d0 = warp * 64 + q4 * 2;
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
@@ -249,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mma_kernel(const DecodeArg
     if (row >= nh) continue;
     const int h = head0 + row;
     const float inv = l[half] > 0.f ? 1.f / l[half] : 1.f;
-    const float lse_v = l[half] > 0.f ? m_run[half] * kLn2 + logf(l[half]) : -INFINITY;
+    const float lse_v = l[half] > 0.f ? mr[half] * kLn2 + logf(l[half]) : -INFINITY;
     if (a.num_splits == 1) {
       OT* o = static_cast<OT*>(a.out) + t * a.out_st + (int64_t)h * a.out_sh + d0;
 #pragma unroll
@@ -312,20 +334,24 @@ __global__ void __launch_bounds__(128) merge_splits_kernel(const DecodeArgs a) {
 }
 
 int launch_decode_mma(const DecodeArgs& a, cudaStream_t st) {
-  const size_t smem = sizeof(Smem);
   // head blocks of one token are adjacent in x so they re-hit the same rows in L2
   dim3 grid((unsigned)(a.T * a.G * a.hb_per_group), a.num_splits);
+  // 32-token chunks pay off once the grid can keep two CTAs on every SM
+  const bool small_chunks = (int64_t)grid.x * grid.y >= 2 * (int64_t)device_sm_count();
   int rc = FP8MLA_OK;
-  auto go = [&](auto kern) {
+  auto go = [&](auto kern, size_t smem) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return check_cuda(e, "decode_mma smem attribute");
     kern<<<grid, kThreads, smem, st>>>(a);
     return check_cuda(cudaGetLastError(), "decode_mma_kernel launch");
   };
+  const size_t s32 = sizeof(Smem<32>), s64 = sizeof(Smem<64>);
   if (a.q_dtype == FP8MLA_DTYPE_BF16)
-    rc = go(decode_mma_kernel<__nv_bfloat16, __nv_bfloat16>);
+    rc = small_chunks ? go(decode_mma_kernel<__nv_bfloat16, __nv_bfloat16, 32>, s32)
+                      : go(decode_mma_kernel<__nv_bfloat16, __nv_bfloat16, 64>, s64);
   else
-    rc = go(decode_mma_kernel<float, float>);
+    rc = small_chunks ? go(decode_mma_kernel<float, float, 32>, s32)
+                      : go(decode_mma_kernel<float, float, 64>, s64);
   if (rc != FP8MLA_OK || a.num_splits == 1) return rc;
   return launch_merge_splits(a, st);
 }

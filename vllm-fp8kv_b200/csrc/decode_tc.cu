@@ -117,22 +117,6 @@ __host__ __device__ constexpr int nv_index(int bi) {
   return bi < 4 * H ? bi : bi - 4;
 }
 
-// Exact bf16(fp32(e4m3) * scale) of the 4 bytes of w: the hardware e4m3x2 ->
-// f16x2 conversion is exact (every e4m3 value, subnormals and NaN included, is
-// an f16), f16 -> f32 is exact, then one fp32 multiply and one RNE cast, as in
-// the reference (fp8_ds_mla_sparse_decode.py:152-164).
-__device__ __forceinline__ void dequant4_hw(uint32_t w, float s, uint32_t& lo, uint32_t& hi) {
-  uint32_t h01, h23;
-  asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n"
-      " cvt.rn.f16x2.e4m3x2 %0, l;\n cvt.rn.f16x2.e4m3x2 %1, h;\n}\n"
-      : "=r"(h01), "=r"(h23)
-      : "r"(w));
-  const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
-  const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
-  lo = pack_bf16x2(f01.x * s, f01.y * s);
-  hi = pack_bf16x2(f23.x * s, f23.y * s);
-}
-
 // One load-warp lane's share of a row: fp8 chunks p + 4i (i = 0..7, chunk i
 // lands in tile block i), rope chunks p and p + 4, and the row's 4 tile scales.
 struct RowPart {
