@@ -131,6 +131,36 @@ FP8MLA_API int fp8mla_sparse_decode(const void* q, int q_dtype, int64_t T, int64
                          int64_t workspace_bytes, void* stream);
 
 /*
+ * The same decode over request-local token positions: the slot of position
+ * tok of query token t is
+ *   block_table[req_id[t] * bt_stride + tok / block_size] * block_size
+ *     + tok % block_size,
+ * -1 (masked) when tok < 0 or tok / block_size >= max_blocks, then masked
+ * like fp8mla_sparse_decode when outside [0, num_slots).  The conversion runs
+ * inside the gather: no [T, topk] slot array is written or read.
+ *
+ * Replaces the pair the reference runs per fp8 layer
+ * (vllm_fp8kv/backend_patch.py:83-89): vLLM's
+ * `triton_convert_req_index_to_global_index` (installed
+ * vllm/v1/attention/backends/mla/sparse_utils.py:85) followed by
+ * `fp8_ds_mla_sparse_decode`.  Bit-identical to fp8mla_convert_req_index then
+ * fp8mla_sparse_decode with the same arguments (int32 arithmetic included).
+ *
+ *   req_id      [T] int32 request of each query token.
+ *   block_table [*, bt_stride] int32 page ids; bt_stride >= max_blocks.
+ *   token_idx   [T, G, topk] int32 request-local positions (strides
+ *               ti_stride_t, ti_stride_g; unit last stride).
+ * Other arguments as fp8mla_sparse_decode.  No topk % 128 requirement.
+ */
+FP8MLA_API int fp8mla_sparse_decode_paged(
+    const void* q, int q_dtype, int64_t T, int64_t H, int64_t q_stride_t, int64_t q_stride_h,
+    const uint8_t* kv, int64_t num_slots, const int32_t* req_id, const int32_t* block_table,
+    int64_t bt_stride, int64_t max_blocks, int64_t block_size, const int32_t* token_idx,
+    int64_t G, int64_t topk, int64_t ti_stride_t, int64_t ti_stride_g, float sm_scale, void* out,
+    int64_t out_stride_t, int64_t out_stride_h, float* lse, int64_t lse_stride_t, int num_splits,
+    void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * fp8mla_sparse_decode for callers that cannot allocate device memory.
  * No counterpart in the reference.  Same arguments and behaviour as
  * fp8mla_sparse_decode minus the workspace: the split-KV scratch comes from a

@@ -12,6 +12,7 @@ from oracle import oracle as O
 from tests import gpu_util as U
 from tests import vllm_fakes
 from vllm_fp8kv import backend_patch, synthetic
+from vllm_fp8kv.index_convert import convert_req_index_to_global_index
 from vllm_fp8kv.fp8_ds_mla_sparse_decode import NOPE, ROPE, ROW_BYTES
 
 
@@ -121,30 +122,28 @@ def test_forward_fp8_kv_accepts_tuple_q_and_slices_heads(vllm, cuda_device):
 
 
 @pytest.mark.gpu
-def test_forward_mqa_dispatch_and_index_conversion(vllm, cuda_device):
+def test_forward_mqa_dispatch_and_fused_index_conversion(vllm, cuda_device):
+    """fp8_ds_mla layers decode straight from request-local positions; the
+    result equals the reference's pair (convert to flat slots, then decode)."""
     backend_patch.apply()
-    seen = {}
-    real = backend_patch._forward_fp8_kv
 
-    def spy(self, q, cache, topk_indices, md):
-        seen["idx"] = topk_indices.clone()
-        return real(self, q, cache, topk_indices, md)
+    class Md:
+        req_id_per_token = torch.zeros(1, dtype=torch.int32, device="cuda")
+        block_table = torch.tensor([[3, 1, 0, 2, 4, 5, 6, 7]], dtype=torch.int32, device="cuda")
+        block_size = 64
+        topk_tokens = 128
 
-    backend_patch._forward_fp8_kv = spy
-    try:
-        class Md:
-            req_id_per_token = torch.zeros(1, dtype=torch.int32, device="cuda")
-            block_table = torch.tensor([[3, 1, 0, 2, 4, 5, 6, 7]], dtype=torch.int32, device="cuda")
-            block_size = 64
-            topk_tokens = 128
-
-        impl = vllm.impl(kv_cache_dtype="fp8_ds_mla", softmax_scale=1 / 24.0)
-        impl.topk_indices_buffer = torch.tensor([[0, 1, 64, -1] + [-1] * 124], dtype=torch.int32,
-                                                device="cuda")
-        q = torch.randn(1, 16, NOPE + ROPE, device="cuda").bfloat16()
-        out, extra = impl.forward_mqa(q, _pool(8 * 64), Md, None)
-    finally:
-        backend_patch._forward_fp8_kv = real
+    impl = vllm.impl(kv_cache_dtype="fp8_ds_mla", softmax_scale=1 / 24.0)
+    impl.topk_indices_buffer = torch.tensor([[0, 1, 64, -1] + [-1] * 124], dtype=torch.int32,
+                                            device="cuda")
+    q = torch.randn(1, 16, NOPE + ROPE, device="cuda").bfloat16()
+    pool = _pool(8 * 64)
+    out, extra = impl.forward_mqa(q, pool, Md, None)
     assert extra is None and impl.bf16_calls == 0
     assert out.shape == (1, 16, NOPE) and torch.isfinite(out.float()).all()
-    assert seen["idx"][0, :4].tolist() == [3 * 64, 3 * 64 + 1, 64, -1]
+    slots = convert_req_index_to_global_index(Md.req_id_per_token, Md.block_table,
+                                              impl.topk_indices_buffer, BLOCK_SIZE=64,
+                                              NUM_TOPK_TOKENS=128)
+    assert slots[0, :4].tolist() == [3 * 64, 3 * 64 + 1, 64, -1]
+    flat = backend_patch._forward_fp8_kv(impl, q, pool, slots, attn_metadata=None)
+    assert torch.equal(out, flat)

@@ -329,3 +329,59 @@ def test_h128_bf16_dispatches_to_tcgen05(cuda_device):
     assert decode_kernel_name(64, 128, 1, 2048, torch.float32) == "decode_mma_kernel"
     assert decode_kernel_name(256, 16, 1, 2048, torch.bfloat16, 8) == \
         "decode_mma_kernel+merge_splits_kernel"
+
+
+# ------------------------------------------------------------ fused block-table conversion
+@pytest.mark.parametrize("H,splits", [(128, 1), (128, 2), (16, 8), (16, None), (64, None)])
+def test_paged_decode_equals_convert_then_decode(cuda_device, H, splits):
+    """fp8mla_sparse_decode_paged == vLLM's converter followed by the flat
+    decode, bit for bit: tokens of one request share a block table, positions
+    past the table and masked positions decode as masked, and the table is a
+    strided view."""
+    from vllm_fp8kv.fp8_ds_mla_sparse_decode import fp8_ds_mla_sparse_decode_paged
+    from vllm_fp8kv.index_convert import convert_req_index_to_global_index
+
+    shape = synthetic.Shape("paged", B=5, H=H, topk=256, ctx=4096, pool_slots=5 * 4096,
+                            mask_frac=0.1)
+    w = synthetic.make_host(shape, seed=H)
+    pool = U.device_pool(w.kv_src_bits, check_against_oracle=False)
+    T = 7
+    rng = np.random.default_rng(H + 1)
+    req = rng.integers(0, shape.B, size=T).astype(np.int32)          # several tokens per request
+    tok = w.token_idx[req].copy()
+    tok[:, 5::37] = shape.ctx + 64 * np.arange(tok[:, 5::37].shape[1])  # blocks past the table
+    wide = np.full((shape.B, w.block_table.shape[1] + 3), 7, dtype=np.int32)
+    wide[:, : w.block_table.shape[1]] = w.block_table
+    bt = torch.from_numpy(wide).cuda()[:, : w.block_table.shape[1]]   # strided view
+    req_t, tok_t = torch.from_numpy(req).cuda(), torch.from_numpy(tok).cuda()
+    q = torch.randn((T, H, 576), generator=torch.Generator().manual_seed(H)).bfloat16().cuda()
+
+    slots = convert_req_index_to_global_index(req_t, bt, tok_t, BLOCK_SIZE=64, NUM_TOPK_TOKENS=256)
+    flat, flat_lse = fp8_ds_mla_sparse_decode(q, pool, slots, w.sm_scale, return_lse=True,
+                                              num_kv_splits=splits)
+    fused, fused_lse = fp8_ds_mla_sparse_decode_paged(q, pool, req_t, bt, tok_t, w.sm_scale,
+                                                      block_size=64, return_lse=True,
+                                                      num_kv_splits=splits)
+    torch.cuda.synchronize()
+    assert torch.equal(fused, flat) and torch.equal(fused_lse, flat_lse)
+
+    ref_slots = O.convert_req_index(req, wide[:, : w.block_table.shape[1]], tok, 64)
+    assert np.array_equal(slots.cpu().numpy(), ref_slots)
+    ref, ref_lse = O.sparse_decode(q.float().cpu().numpy(), pool.view(-1, 656).cpu().numpy(),
+                                   ref_slots, w.sm_scale)
+    U.assert_close(fused.float().cpu().numpy(), ref)
+    U.assert_lse_close(fused_lse.cpu().numpy(), ref_lse)
+
+
+def test_paged_decode_rejects_bad_tables(cuda_device):
+    from vllm_fp8kv.fp8_ds_mla_sparse_decode import fp8_ds_mla_sparse_decode_paged
+
+    q = torch.zeros((1, 16, 576), dtype=torch.bfloat16, device="cuda")
+    pool = torch.zeros((4, 64, ROW_BYTES), dtype=torch.uint8, device="cuda")
+    req = torch.zeros(1, dtype=torch.int32, device="cuda")
+    tok = torch.zeros((1, 128), dtype=torch.int32, device="cuda")
+    bt = torch.zeros((1, 4), dtype=torch.int32, device="cuda")
+    with pytest.raises(AssertionError):
+        fp8_ds_mla_sparse_decode_paged(q, pool, req, bt, tok, 0.1, block_size=0)
+    with pytest.raises(AssertionError):
+        fp8_ds_mla_sparse_decode_paged(q, pool, req.long(), bt, tok, 0.1)

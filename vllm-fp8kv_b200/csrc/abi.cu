@@ -142,12 +142,23 @@ const char* fp8mla_decode_kernel_name(int64_t T, int64_t H, int64_t G, int64_t t
   return tc ? "decode_tc_kernel" : "decode_mma_kernel";
 }
 
-int fp8mla_sparse_decode(const void* q, int q_dtype, int64_t T, int64_t H, int64_t q_stride_t,
-                         int64_t q_stride_h, const uint8_t* kv, int64_t num_slots,
-                         const int32_t* indices, int64_t G, int64_t topk, int64_t idx_stride_t,
-                         int64_t idx_stride_g, float sm_scale, void* out, int64_t out_stride_t,
-                         int64_t out_stride_h, float* lse, int64_t lse_stride_t, int num_splits,
-                         void* workspace, int64_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Block-table indirection of fp8mla_sparse_decode_paged (null for flat slots).
+struct PagedIndex {
+  const int32_t* req_id;
+  const int32_t* block_table;
+  int64_t bt_stride, max_blocks, block_size;
+};
+
+int decode_impl(const void* q, int q_dtype, int64_t T, int64_t H, int64_t q_stride_t,
+                int64_t q_stride_h, const uint8_t* kv, int64_t num_slots, const int32_t* indices,
+                int64_t G, int64_t topk, int64_t idx_stride_t, int64_t idx_stride_g,
+                float sm_scale, void* out, int64_t out_stride_t, int64_t out_stride_h, float* lse,
+                int64_t lse_stride_t, int num_splits, void* workspace, int64_t workspace_bytes,
+                void* stream, const PagedIndex* paged) {
   g_last_error[0] = 0;
   if (q_dtype != FP8MLA_DTYPE_BF16 && q_dtype != FP8MLA_DTYPE_F32)
     return set_error(FP8MLA_ERR_INVALID_ARGUMENT,
@@ -213,9 +224,54 @@ int fp8mla_sparse_decode(const void* q, int q_dtype, int64_t T, int64_t H, int64
     a.ws_lse = reinterpret_cast<float*>(static_cast<char*>(workspace) +
                                         ((T * H * S * kNope * 4 + 255) / 256) * 256);
   }
+  if (paged != nullptr) {
+    a.req_id = paged->req_id;
+    a.block_table = paged->block_table;
+    a.bt_stride = paged->bt_stride;
+    a.max_blocks = paged->max_blocks;
+    a.block_size = (int)paged->block_size;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (decode_tc_supported(a)) return launch_decode_tc(a, st);
   return launch_decode_mma(a, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int fp8mla_sparse_decode(const void* q, int q_dtype, int64_t T, int64_t H, int64_t q_stride_t,
+                         int64_t q_stride_h, const uint8_t* kv, int64_t num_slots,
+                         const int32_t* indices, int64_t G, int64_t topk, int64_t idx_stride_t,
+                         int64_t idx_stride_g, float sm_scale, void* out, int64_t out_stride_t,
+                         int64_t out_stride_h, float* lse, int64_t lse_stride_t, int num_splits,
+                         void* workspace, int64_t workspace_bytes, void* stream) {
+  return decode_impl(q, q_dtype, T, H, q_stride_t, q_stride_h, kv, num_slots, indices, G, topk,
+                     idx_stride_t, idx_stride_g, sm_scale, out, out_stride_t, out_stride_h, lse,
+                     lse_stride_t, num_splits, workspace, workspace_bytes, stream, nullptr);
+}
+
+int fp8mla_sparse_decode_paged(const void* q, int q_dtype, int64_t T, int64_t H,
+                               int64_t q_stride_t, int64_t q_stride_h, const uint8_t* kv,
+                               int64_t num_slots, const int32_t* req_id,
+                               const int32_t* block_table, int64_t bt_stride, int64_t max_blocks,
+                               int64_t block_size, const int32_t* token_idx, int64_t G,
+                               int64_t topk, int64_t ti_stride_t, int64_t ti_stride_g,
+                               float sm_scale, void* out, int64_t out_stride_t,
+                               int64_t out_stride_h, float* lse, int64_t lse_stride_t,
+                               int num_splits, void* workspace, int64_t workspace_bytes,
+                               void* stream) {
+  g_last_error[0] = 0;
+  if (block_size <= 0 || block_size > (1 << 20) || max_blocks < 0 || bt_stride < max_blocks)
+    return set_error(FP8MLA_ERR_INVALID_ARGUMENT,
+                     "bad block table: block_size=%lld max_blocks=%lld stride=%lld",
+                     (long long)block_size, (long long)max_blocks, (long long)bt_stride);
+  if (T > 0 && topk > 0 && (req_id == nullptr || (max_blocks > 0 && block_table == nullptr)))
+    return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "req_id and block_table are required");
+  const PagedIndex paged{req_id, block_table, bt_stride, max_blocks, block_size};
+  return decode_impl(q, q_dtype, T, H, q_stride_t, q_stride_h, kv, num_slots, token_idx, G, topk,
+                     ti_stride_t, ti_stride_g, sm_scale, out, out_stride_t, out_stride_h, lse,
+                     lse_stride_t, num_splits, workspace, workspace_bytes, stream, &paged);
 }
 
 int fp8mla_ds_mla_write(const uint16_t* kv_c, int64_t kv_c_stride, const uint16_t* k_pe,

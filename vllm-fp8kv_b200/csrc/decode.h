@@ -26,7 +26,37 @@ struct DecodeArgs {
   int split_len;     // top-k entries per split (last split may be shorter)
   float* ws_o;       // [T][H][S][512] fp32 normalised split outputs
   float* ws_lse;     // [T][H][S] natural-log split LSE
+  // Optional block-table indirection (fp8mla_sparse_decode_paged): when
+  // block_table is set, idx holds request-local token positions and the slot
+  // of position tok of token t is block_table[req_id[t], tok / block_size] *
+  // block_size + tok % block_size (-1 for tok < 0 or a block past max_blocks).
+  const int32_t* req_id;
+  const int32_t* block_table;
+  int64_t bt_stride;
+  int64_t max_blocks;
+  int block_size;
 };
+
+#ifdef __CUDACC__
+// The live slot an index entry names, or -1 (masked, past the table, or
+// outside [0, num_slots)).  `req` is req_id[t] when a block table is set.
+// The block-table step is vLLM's converter with its int32 arithmetic
+// (installed vllm/v1/attention/backends/mla/sparse_utils.py:11-78; the
+// library's standalone form is convert_req_index_kernel).
+__device__ __forceinline__ int32_t live_slot(const DecodeArgs& a, int32_t req, int32_t v) {
+  if (a.block_table != nullptr) {
+    if (v < 0) return -1;
+    const int32_t blk = v / a.block_size, off = v - blk * a.block_size;
+    if (blk >= a.max_blocks) return -1;
+    const uint32_t base = (uint32_t)a.block_table[(int64_t)req * a.bt_stride + blk];
+    v = (int32_t)(base * (uint32_t)a.block_size + (uint32_t)off);
+  }
+  return (v >= 0 && (int64_t)v < a.num_slots) ? v : -1;
+}
+__device__ __forceinline__ int32_t request_of(const DecodeArgs& a, int64_t t) {
+  return a.block_table != nullptr ? a.req_id[t] : 0;
+}
+#endif
 
 int launch_decode_mma(const DecodeArgs& a, cudaStream_t st);
 int launch_merge_splits(const DecodeArgs& a, cudaStream_t st);

@@ -61,15 +61,12 @@ static_assert(offsetof(Smem<32>, raw) % 16 == 0 && offsetof(Smem<64>, raw) % 16 
 
 template <int BN>
 __device__ __forceinline__ void issue_gather(Smem<BN>& s, int buf, const DecodeArgs& a,
-                                             const int32_t* idx_row, int pos0, int end) {
+                                             const int32_t* idx_row, int32_t req, int pos0,
+                                             int end) {
   constexpr int kRT = Cfg<BN>::kRowThreads;
   const int r = threadIdx.x / kRT, sub = threadIdx.x % kRT;
   const int pos = pos0 + r;
-  int64_t slot = -1;
-  if (pos < end) {
-    int32_t v = idx_row[pos];
-    if (v >= 0 && (int64_t)v < a.num_slots) slot = v;
-  }
+  const int64_t slot = pos < end ? live_slot(a, req, idx_row[pos]) : -1;
   const bool ok = slot >= 0;
   const uint8_t* src = a.kv + (ok ? slot : 0) * (int64_t)kRowBytes;
   const uint32_t dst = smem_u32(&s.raw[buf][r * kRowBytes]);
@@ -100,11 +97,12 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::kMinBlocks)
   const int beg = split * a.split_len;
   const int end = min(a.topk, beg + a.split_len);
   const int32_t* idx_row = a.idx + t * a.idx_st + grp * a.idx_sg;
+  const int32_t req = request_of(a, t);
 
   const int nchunks = end > beg ? (end - beg + kBN - 1) / kBN : 0;
-  if (nchunks > 0) issue_gather(s, 0, a, idx_row, beg, end);
+  if (nchunks > 0) issue_gather(s, 0, a, idx_row, req, beg, end);
   cp_async_commit();
-  if (nchunks > 1) issue_gather(s, 1, a, idx_row, beg + kBN, end);
+  if (nchunks > 1) issue_gather(s, 1, a, idx_row, req, beg + kBN, end);
   cp_async_commit();
 
   // ---- Q -> smem (bf16), zero rows for padded heads
@@ -169,7 +167,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::kMinBlocks)
 #pragma unroll
     for (int u = 0; u < kTPT; ++u) vt[u] = s.valid[buf][kTPT * sp2 + u] != 0;
     __syncthreads();
-    if (c + 2 < nchunks) issue_gather(s, buf, a, idx_row, beg + (c + 2) * kBN, end);
+    if (c + 2 < nchunks) issue_gather(s, buf, a, idx_row, req, beg + (c + 2) * kBN, end);
     cp_async_commit();
 
     // ---- partial S = Q K^T: tokens 8(w % (BN/8))..+7, d share w / (BN/8)

@@ -128,6 +128,7 @@ struct RowPart {
 struct Ctx {
   const DecodeArgs* a;
   const int32_t* idx_row;
+  int32_t req;  // request of this token (block-table indirection only)
   int beg, end, ntiles;
   uint32_t tmem;
   uint32_t sq, sv0, snv;
@@ -235,9 +236,7 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
   // the live slot of this lane's row of tile jt, or -1 (masked, out of range, past the end)
   auto slot_of = [&](int jt) -> int32_t {
     const int pos = c.beg + jt * kN + row;
-    if (pos >= c.end) return -1;
-    const int32_t v = c.idx_row[pos];
-    return (v >= 0 && (int64_t)v < a.num_slots) ? v : -1;
+    return pos < c.end ? live_slot(a, c.req, c.idx_row[pos]) : -1;
   };
   auto load = [&](int32_t slot, RowPart& P, bool& valid) {
     valid = slot >= 0;
@@ -333,6 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
   c.end = min(a.topk, c.beg + a.split_len);
   c.ntiles = c.end > c.beg ? (c.end - c.beg + kN - 1) / kN : 0;
   c.idx_row = a.idx + t * a.idx_st + grp * a.idx_sg;
+  c.req = request_of(a, t);
   c.sq = smem_u32(s.q);
   c.sv0 = smem_u32(s.v[0]);
   c.snv = smem_u32(s.nv);

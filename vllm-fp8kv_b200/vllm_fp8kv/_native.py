@@ -38,6 +38,14 @@ SIGNATURES = {
         _P, _I64, _I64,                        # out, out strides
         _P, _I64,                              # lse, lse stride
         _I32, _P, _I64, _P]),                  # num_splits, workspace, bytes, stream
+    "fp8mla_sparse_decode_paged": (_I32, [
+        _P, _I32, _I64, _I64, _I64, _I64,      # q, q_dtype, T, H, q strides
+        _P, _I64,                              # kv, num_slots
+        _P, _P, _I64, _I64, _I64,              # req_id, block_table, bt stride, max_blocks, block_size
+        _P, _I64, _I64, _I64, _I64,            # token_idx, G, topk, token_idx strides
+        _F32,                                  # sm_scale
+        _P, _I64, _I64, _P, _I64,              # out, out strides, lse, lse stride
+        _I32, _P, _I64, _P]),                  # num_splits, workspace, bytes, stream
     "fp8mla_sparse_decode_noalloc": (_I32, [
         _P, _I32, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _F32,
         _P, _I64, _I64, _P, _I64, _I32, _P]),

@@ -4,9 +4,11 @@ Behaviour matches the reference's backend_patch (vllm_fp8kv/backend_patch.py:50-
 
 * ``_forward_fp8_kv``            -- decode over flat global slots; q may be a
                                     (nope, rope) tuple; heads sliced to the layer's count
+* ``_forward_fp8_kv_paged``      -- the same decode over request-local top-k
+                                    positions: the block-table conversion runs
+                                    inside the decode's gather (one launch)
 * ``_forward_mqa_fp8_aware``     -- replaces ``forward_mqa``: fp8_ds_mla goes to
-                                    the sm_100a decode (slot conversion by the
-                                    library's CUDA converter), everything else to
+                                    the fused sm_100a decode, everything else to
                                     upstream's bf16 path with upstream's converter
 * ``_get_kv_cache_shape_fp8_aware`` -- 656-byte rows for fp8_ds_mla
 * ``_patch_mla_spec_quant_mode`` -- the MLA KV-cache spec of an fp8_ds_mla pool
@@ -16,8 +18,11 @@ Behaviour matches the reference's backend_patch (vllm_fp8kv/backend_patch.py:50-
 
 import torch
 
-from vllm_fp8kv.fp8_ds_mla_sparse_decode import ROW_BYTES, fp8_ds_mla_sparse_decode
-from vllm_fp8kv.index_convert import convert_req_index_to_global_index
+from vllm_fp8kv.fp8_ds_mla_sparse_decode import (
+    ROW_BYTES,
+    fp8_ds_mla_sparse_decode,
+    fp8_ds_mla_sparse_decode_paged,
+)
 
 FP8_DS_MLA = "fp8_ds_mla"
 _CLI_FP8_NAMES = ("fp8", "fp8_e4m3")
@@ -37,6 +42,23 @@ def _forward_fp8_kv(self, q, kv_c_and_k_pe_cache, topk_indices, attn_metadata):
     return out[:, : self.num_heads, :]
 
 
+def _forward_fp8_kv_paged(self, q, kv_c_and_k_pe_cache, topk_indices, attn_metadata):
+    """Decode over fp8_ds_mla pages from request-local top-k positions.
+
+    Same result as converting with ``triton_convert_req_index_to_global_index``
+    and calling ``_forward_fp8_kv`` (the reference's pair,
+    vllm_fp8kv/backend_patch.py:83-89); the conversion happens in the gather.
+    """
+    q = _as_single_q(q)
+    n_tok = q.shape[0]
+    md = attn_metadata
+    out = fp8_ds_mla_sparse_decode_paged(
+        q, kv_c_and_k_pe_cache, md.req_id_per_token[:n_tok].to(torch.int32).contiguous(),
+        md.block_table.to(torch.int32), topk_indices.view(n_tok, 1, -1),
+        sm_scale=self.softmax_scale, block_size=md.block_size)
+    return out[:, : self.num_heads, :]
+
+
 def _forward_mqa_fp8_aware(self, q, kv_c_and_k_pe_cache, attn_metadata, layer):
     """Replacement ``forward_mqa`` that accepts fp8_ds_mla KV."""
     q = _as_single_q(q)
@@ -45,10 +67,7 @@ def _forward_mqa_fp8_aware(self, q, kv_c_and_k_pe_cache, attn_metadata, layer):
     topk_indices = self.topk_indices_buffer[:n_tok]
     md = attn_metadata
     if self.kv_cache_dtype == FP8_DS_MLA:
-        slots = convert_req_index_to_global_index(
-            md.req_id_per_token, md.block_table, topk_indices,
-            BLOCK_SIZE=md.block_size, NUM_TOPK_TOKENS=md.topk_tokens)
-        attn_out = _forward_fp8_kv(self, q, kv_c_and_k_pe_cache, slots, md)
+        attn_out = _forward_fp8_kv_paged(self, q, kv_c_and_k_pe_cache, topk_indices, md)
     else:
         from vllm.v1.attention.backends.mla.xpu_mla_sparse import (
             triton_convert_req_index_to_global_index,

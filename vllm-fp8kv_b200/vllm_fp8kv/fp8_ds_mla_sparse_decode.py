@@ -123,3 +123,80 @@ def fp8_ds_mla_sparse_decode(
         splits, ws_ptr, ws_bytes, N.stream_ptr(q.device))
     N.check(rc, "fp8_ds_mla_sparse_decode")
     return (out, lse) if return_lse else out
+
+
+def fp8_ds_mla_sparse_decode_paged(
+    q: torch.Tensor,             # [seq_q, h_q, 576]  bf16 (fp32 allowed for tests)
+    kv_cache: torch.Tensor,      # [num_blocks, block_size, 656] uint8 / float8_e4m3fn, contiguous
+    req_id: torch.Tensor,        # [seq_q] int32: request of each query token
+    block_table: torch.Tensor,   # [num_reqs, max_blocks] int32 page ids
+    token_indices: torch.Tensor, # [seq_q, kv_groups, topk] or [seq_q, topk] int32; -1 = masked
+    sm_scale: float,
+    block_size: int = 64,
+    return_lse: bool = False,
+    *,
+    num_kv_splits: int | None = None,
+    workspace: torch.Tensor | None = None,
+):
+    """`fp8_ds_mla_sparse_decode` over request-local token positions.
+
+    Equivalent to converting `token_indices` with vLLM's
+    `triton_convert_req_index_to_global_index(req_id, block_table,
+    token_indices, BLOCK_SIZE=block_size)` and decoding the flat slots (the
+    pair the reference runs per layer, vllm_fp8kv/backend_patch.py:83-89), but
+    the conversion happens inside the decode's gather: no slot tensor is
+    materialised and there is no separate launch.  Results are bit-identical
+    to that pair.
+    """
+    assert kv_cache.dtype in (torch.uint8, torch.float8_e4m3fn), kv_cache.dtype
+    assert kv_cache.is_contiguous(), "kv_cache must be contiguous"
+    assert q.stride(-1) == 1 and token_indices.stride(-1) == 1, "need unit last-dim strides"
+    assert q.dtype in (torch.bfloat16, torch.float32), (
+        f"rope is stored bf16; q must be bf16 (fp32 allowed for testing), got {q.dtype}"
+    )
+    assert req_id.dtype == torch.int32 and block_table.dtype == torch.int32, "int32 tables"
+    assert token_indices.dtype == torch.int32, f"indices must be int32, got {token_indices.dtype}"
+    assert block_table.dim() == 2 and block_table.stride(1) == 1, "block_table [reqs, max_blocks]"
+    assert req_id.dim() == 1 and req_id.shape[0] == q.shape[0] and req_id.is_contiguous()
+    assert block_size > 0
+    kv_u8 = kv_cache.view(torch.uint8).reshape(-1, ROW_BYTES)
+    num_slots = kv_u8.shape[0]
+
+    seq_q, h_q, dim_qk = q.shape
+    assert dim_qk == NOPE + ROPE, f"expected {NOPE + ROPE}, got {dim_qk}"
+    if token_indices.dim() == 2:
+        token_indices = token_indices.unsqueeze(1)
+    kv_groups, topk = token_indices.shape[1], token_indices.shape[2]
+    assert h_q % kv_groups == 0, f"h_q={h_q} not divisible by kv_groups={kv_groups}"
+    N.require_cuda(q, kv_u8, token_indices, req_id, block_table)
+
+    vec = 8 if q.dtype == torch.bfloat16 else 4
+    if q.data_ptr() % 16 or q.stride(0) % vec or q.stride(1) % vec:
+        q = q.contiguous()
+        if q.data_ptr() % 16:
+            q = q.clone()
+
+    out = torch.empty((seq_q, h_q, NOPE), dtype=q.dtype, device=q.device)
+    lse = torch.empty((seq_q, h_q), dtype=torch.float32, device=q.device) if return_lse else None
+
+    splits = 0 if num_kv_splits is None else int(num_kv_splits)
+    need = decode_workspace_bytes(seq_q, h_q, kv_groups, topk, splits)
+    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_ptr = workspace.data_ptr() if (need and workspace is not None) else None
+    ws_bytes = workspace.numel() * workspace.element_size() if (need and workspace is not None) else 0
+
+    rc = N.lib().fp8mla_sparse_decode_paged(
+        q.data_ptr(), N.DTYPE_BF16 if q.dtype == torch.bfloat16 else N.DTYPE_F32,
+        seq_q, h_q, q.stride(0), q.stride(1),
+        kv_u8.data_ptr(), num_slots,
+        req_id.data_ptr(), block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
+        int(block_size),
+        token_indices.data_ptr(), kv_groups, topk, token_indices.stride(0),
+        token_indices.stride(1),
+        float(sm_scale),
+        out.data_ptr(), out.stride(0), out.stride(1),
+        lse.data_ptr() if lse is not None else None, lse.stride(0) if lse is not None else 0,
+        splits, ws_ptr, ws_bytes, N.stream_ptr(q.device))
+    N.check(rc, "fp8_ds_mla_sparse_decode_paged")
+    return (out, lse) if return_lse else out
