@@ -37,6 +37,8 @@
 //               reduction.  The reference max is only raised when a tile
 //               exceeds it by more than 8 (log2 units); P <= 2^8 keeps its
 //               bf16 precision and the final 1/l and LSE use the same max.
+//               S is read from tensor memory twice, 32 columns at a time (the
+//               max, then the exponentials): small code and few registers.
 //   warp 4      TMEM allocation and the single-thread MMA issuer
 //   warps 5-12  gather + dequant: each warp owns 8 of the 64 rows of a tile
 //               (4 lanes per row) and loads them straight into registers one
@@ -417,18 +419,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
       if (!ok) break;
       tc_fence_after();
       const uint32_t sb = trow + kColS + kSBufCols * b;
-      uint32_t s0[32], s1[32];
-      tmem_ld32(sb, s0);
-      tmem_ld32(sb + 32, s1);
       const uint2 vbw = *reinterpret_cast<const uint2*>(s.vbits[vs]);  // bit k = token k
-      tmem_wait_ld();
-      float x[64];
+      // pass 1: the tile max (rolled over the two 32-token halves: small code)
       float tmax = -INFINITY;
+#pragma unroll 1
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t sv[32];
+        tmem_ld32(sb + 32 * hf, sv);
+        tmem_wait_ld();
+        const uint32_t vm = hf ? vbw.y : vbw.x;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        x[i] = ((vbw.x >> i) & 1u) ? __uint_as_float(s0[i]) * a.scale_log2 : -INFINITY;
-        x[32 + i] = ((vbw.y >> i) & 1u) ? __uint_as_float(s1[i]) * a.scale_log2 : -INFINITY;
-        tmax = fmaxf(tmax, fmaxf(x[i], x[32 + i]));
+        for (int i = 0; i < 32; ++i)
+          if ((vm >> i) & 1u) tmax = fmaxf(tmax, __uint_as_float(sv[i]) * a.scale_log2);
       }
       // lazy reference max: raise it only when this tile exceeds it by > threshold
       float alpha = 1.f;
@@ -454,14 +456,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const DecodeArgs
       }
       // nothing valid yet: every x is -inf, use 0 so exp2(-inf - ref) is 0, not NaN
       const float mref = (m_used == -INFINITY) ? 0.f : m_used;
-      uint32_t pk[32];
+      // pass 2: P for tokens 32hf..+31 over packed columns 16hf..+15 (their S was read)
+#pragma unroll 1
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t sv[32];
+        tmem_ld32(sb + 32 * hf, sv);
+        tmem_wait_ld();
+        const uint32_t vm = hf ? vbw.y : vbw.x;
+        uint32_t pk[16];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float p0 = ex2_approx(x[2 * i] - mref), p1 = ex2_approx(x[2 * i + 1] - mref);
-        l += p0 + p1;
-        pk[i] = pack_bf16x2(p0, p1);
+        for (int i = 0; i < 16; ++i) {
+          const float x0 = ((vm >> (2 * i)) & 1u) ? __uint_as_float(sv[2 * i]) * a.scale_log2 : -INFINITY;
+          const float x1 =
+              ((vm >> (2 * i + 1)) & 1u) ? __uint_as_float(sv[2 * i + 1]) * a.scale_log2 : -INFINITY;
+          const float p0 = ex2_approx(x0 - mref), p1 = ex2_approx(x1 - mref);
+          l += p0 + p1;
+          pk[i] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(sb + 16 * hf, pk);
       }
-      tmem_st32(sb, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(c.b_pfull + 8 * b);
