@@ -11,7 +11,9 @@ step time is the max over ranks.  Rank 0 prints one JSON line.
 
 value      = KV GB/s of the whole job = (N * B * topk * 656 bytes) / step time
 e2e        = same metric through the public Python API with the step's q and
-             indices copied from pinned host memory and out copied back
+             indices copied from pinned host memory and out copied back, each
+             direction on its own stream (double-buffered) so step i's copies
+             overlap the decode of its neighbours, as a serving loop runs
 roofline   = the decode kernel's achieved TFLOP/s (or GB/s for the HBM-bound
              shapes) from CUDA events on its stream, against MEASURED_PEAKS.json
 cpu_baseline = the oracle's numpy restatement of the reference's fp32 torch
@@ -257,37 +259,66 @@ def run_ours(args, rank, world, local_rank):
     launch_ms = float(np.mean([a.elapsed_time(b) for a, b in zip(starts, ends)]))
     step_ms = window_ms / args.steps
 
-    # ---- end to end through the public API: pinned host q/indices in, out back
+    # ---- end to end through the public API: pinned host q/indices in, out back.
+    # Copies run on their own streams (one per PCIe direction), double-buffered:
+    # the H2D of step i+1 and the D2H of step i-1 overlap the decode of step i.
     hq = [sq.cpu().pin_memory() for sq, _ in sets]
     hi = [sl.cpu().pin_memory() for _, sl in sets]
-    hout = torch.empty((s.B, s.H, 512), dtype=torch.bfloat16).pin_memory()
-    hlse = torch.empty((s.B, s.H), dtype=torch.float32).pin_memory()
-    dq = [torch.empty_like(sq) for sq, _ in sets]
-    di = [torch.empty_like(sl) for _, sl in sets]
+    hout = [torch.empty((s.B, s.H, 512), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    hlse = [torch.empty((s.B, s.H), dtype=torch.float32).pin_memory() for _ in range(2)]
+    dq = [torch.empty_like(sets[0][0]) for _ in range(2)]
+    di = [torch.empty_like(sets[0][1]) for _ in range(2)]
+    copy_in = torch.cuda.Stream(dev)
+    copy_out = torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    out_done = [torch.cuda.Event() for _ in range(2)]   # D2H of buffer b finished
+    inputs_free = [torch.cuda.Event() for _ in range(2)]  # decode of buffer b consumed dq/di
 
-    def e2e_step(i):
-        k = i % N_SETS
-        dq[k].copy_(hq[k], non_blocking=True)
-        di[k].copy_(hi[k], non_blocking=True)
-        out, lse = fp8_ds_mla_sparse_decode(dq[k], kv, di[k], w.sm_scale, return_lse=True,
-                                            num_kv_splits=splits, workspace=ws)
-        hout.copy_(out, non_blocking=True)
-        hlse.copy_(lse, non_blocking=True)
+    def h2d(i):
+        b, k = i & 1, i % N_SETS
+        with torch.cuda.stream(copy_in):
+            copy_in.wait_event(inputs_free[b])
+            dq[b].copy_(hq[k], non_blocking=True)
+            di[b].copy_(hi[k], non_blocking=True)
+            in_ready[b].record(copy_in)
 
-    for i in range(args.warmup):
-        e2e_step(i)
+    def e2e_run(n):
+        for ev in inputs_free + out_done:
+            ev.record(stream)
+        h2d(0)
+        for i in range(n):
+            b = i & 1
+            if i + 1 < n:
+                h2d(i + 1)
+            stream.wait_event(in_ready[b])
+            stream.wait_event(out_done[b])  # hout[b] / the previous out of buffer b are free
+            out, lse = fp8_ds_mla_sparse_decode(dq[b], kv, di[b], w.sm_scale, return_lse=True,
+                                                num_kv_splits=splits, workspace=ws)
+            inputs_free[b].record(stream)
+            done = torch.cuda.Event()
+            done.record(stream)
+            with torch.cuda.stream(copy_out):
+                copy_out.wait_event(done)
+                out.record_stream(copy_out)
+                lse.record_stream(copy_out)
+                hout[b].copy_(out, non_blocking=True)
+                hlse[b].copy_(lse, non_blocking=True)
+                out_done[b].record(copy_out)
+        stream.wait_stream(copy_in)
+        stream.wait_stream(copy_out)
+
+    e2e_run(args.warmup)
     torch.cuda.synchronize(dev)
     if dist:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
-        e2e_step(i)
+    e2e_run(args.steps)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1) / args.steps
-    h2d = sets[0][0].numel() * 2 + sets[0][1].numel() * 4
-    d2h = hout.numel() * 2 + hlse.numel() * 4
+    h2d_b = sets[0][0].numel() * 2 + sets[0][1].numel() * 4
+    d2h_b = hout[0].numel() * 2 + hlse[0].numel() * 4
 
     # ---- max over ranks (no collective on the hot path; this is after timing)
     vals = torch.tensor([step_ms, e2e_ms, launch_ms], dtype=torch.float64, device=dev)
@@ -342,8 +373,8 @@ def run_ours(args, rank, world, local_rank):
             "tflops": world * flops / (step_ms * 1e-3) / 1e12,
             "roofline": roof,
             "e2e": {"value": world * kvb / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
-                    "us_per_call": e2e_ms * 1e3, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+                    "us_per_call": e2e_ms * 1e3, "h2d_bytes_per_step": h2d_b,
+                    "d2h_bytes_per_step": d2h_b},
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clk.summary(),
         }
