@@ -214,6 +214,20 @@ FP8MLA_API int fp8mla_dequant_e4m3(const uint8_t* in, int64_t n, void* out,
                         int out_dtype, int method, void* stream);
 
 /*
+ * Gather + dequant of n fp8_ds_mla rows by slot into bf16 out[n, 576]
+ * (row stride out_stride elements, >= 576, 16-byte aligned):
+ * out[r, d] = bf16(float(e4m3 latent[d]) * scale[d / 128]) for d < 512 and the
+ * raw rope for d >= 512; slot < 0 or >= num_slots gives a zero row.  It runs
+ * the decode kernels' own device dequant (method 0: the general kernel's,
+ * 1: the tcgen05 kernel's) so that both can be checked bit for bit.
+ * Replaces the IS_FP8 gather + dequant inside `_fp8_ds_mla_sparse_decode_kernel`
+ * (vllm_fp8kv/fp8_ds_mla_sparse_decode.py:136-168).
+ */
+FP8MLA_API int fp8mla_ds_mla_dequant_rows(const uint8_t* kv, int64_t num_slots,
+                               const int32_t* slots, int64_t n, uint16_t* out,
+                               int64_t out_stride, int method, void* stream);
+
+/*
  * Token-relative top-k -> flat global slot:
  *   out[t, i] = block_table[req_id[t], tok / block_size] * block_size
  *               + tok % block_size,  with tok = token_idx[t, i];

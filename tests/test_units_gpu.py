@@ -13,7 +13,8 @@ from tests import gpu_util as U
 from tests.conftest import golden
 from vllm_fp8kv import synthetic
 from vllm_fp8kv.cache_writer import concat_and_cache_ds_mla, concat_and_cache_mla
-from vllm_fp8kv.fp8_dequant import build_lut, dequant_device, dequant_triton_launch
+from vllm_fp8kv.fp8_dequant import (build_lut, dequant_device, dequant_ds_mla_rows,
+                                     dequant_triton_launch)
 from vllm_fp8kv.index_convert import convert_req_index_to_global_index
 
 pytestmark = pytest.mark.gpu
@@ -50,6 +51,54 @@ def test_dequant_denormals_and_signed_zero(cuda_device):
         ref = b.view(torch.float8_e4m3fn).to(torch.float16)
         assert torch.equal(out, ref)
         assert torch.signbit(out[3]), "-0.0 lost its sign"
+
+
+def _rows_with_all_bytes_and_scales(scales):
+    """One fp8_ds_mla row per scale: latent = all 256 bytes twice, the same
+    scale in all four tiles, rope random bf16 bits."""
+    n = len(scales)
+    rows = np.zeros((n, 656), dtype=np.uint8)
+    rows[:, :512] = np.concatenate([np.arange(256), np.arange(256)[::-1]]).astype(np.uint8)
+    rows[:, 512:528] = np.repeat(np.asarray(scales, dtype=np.float32)[:, None], 4, 1).view(np.uint8)
+    rng = np.random.default_rng(7)
+    rope = rng.standard_normal((n, 64)).astype(np.float32)
+    rows[:, 528:] = torch.from_numpy(rope).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint8)
+    return rows
+
+
+@pytest.mark.parametrize("method", [0, 1])
+def test_decode_row_dequant_bit_exact_all_bytes_and_scales(cuda_device, method):
+    # scales: typical amax/448, the extreme tiles of the edge-case workload
+    # (amax 1e-4 .. 1e4), exact zero, a power of two, products that land in
+    # bf16's subnormal range and ones that overflow to inf
+    scales = [1.0, 2.0 ** -7, 2.3 / 448, 1e-4 / 448, 1e4 / 448, 0.0, 3.1e-38, 1e-30, 7.7e35,
+              1.7e38, 0.1234567]
+    rows = _rows_with_all_bytes_and_scales(scales)
+    kv = torch.from_numpy(rows).cuda()
+    n = len(scales)
+    slots = torch.tensor(list(range(n)) + [-1, n, 2 ** 31 - 1], dtype=torch.int32, device="cuda")
+    got = dequant_ds_mla_rows(kv, slots, method)
+    torch.cuda.synchronize()
+    lat = torch.from_numpy(rows[:, :512].copy()).view(torch.float8_e4m3fn).float()
+    sc = torch.from_numpy(rows[:, 512:528].copy()).view(torch.float32)       # [n, 4]
+    want = (lat.view(n, 4, 128) * sc[:, :, None]).view(n, 512).to(torch.bfloat16)
+    g = got[:n, :512].cpu()
+    assert torch.equal(torch.isnan(g), torch.isnan(want)), "NaN positions differ"
+    fin = ~torch.isnan(want)
+    assert torch.equal(g.view(torch.int16)[fin], want.view(torch.int16)[fin])
+    assert np.array_equal(got[:n, 512:].cpu().view(torch.uint8).numpy().reshape(n, 128),
+                          rows[:, 528:])
+    assert not got[n:].any(), "masked / out-of-range slots must give zero rows"
+
+
+def test_decode_row_dequant_methods_agree_on_synthetic_pool(cuda_device):
+    # the edge-case workload's value distribution: tile amax 1e-4 .. 1e4 and zero tiles
+    w = synthetic.make_device("c4", seed=3, device="cuda", B=1, pool_slots=1 << 17)
+    n = w.kv.numel() // 656
+    slots = torch.arange(-1, n + 1, dtype=torch.int32, device="cuda")
+    a = dequant_ds_mla_rows(w.kv, slots, 0)
+    b = dequant_ds_mla_rows(w.kv, slots, 1)
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
 
 
 @pytest.mark.parametrize("n", [300, 1 << 20])

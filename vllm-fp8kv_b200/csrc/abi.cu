@@ -300,6 +300,23 @@ int fp8mla_dequant_e4m3(const uint8_t* in, int64_t n, void* out, int out_dtype, 
   return launch_dequant(in, n, out, out_dtype, method, static_cast<cudaStream_t>(stream));
 }
 
+int fp8mla_ds_mla_dequant_rows(const uint8_t* kv, int64_t num_slots, const int32_t* slots,
+                               int64_t n, uint16_t* out, int64_t out_stride, int method,
+                               void* stream) {
+  g_last_error[0] = 0;
+  if (n < 0 || num_slots < 0 || (method != 0 && method != 1) || out_stride < kDqk)
+    return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "bad row-dequant arguments");
+  if (n == 0) return FP8MLA_OK;
+  if (kv == nullptr || slots == nullptr || out == nullptr)
+    return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "null row-dequant pointer");
+  if ((reinterpret_cast<uintptr_t>(kv) | reinterpret_cast<uintptr_t>(out) |
+       (uintptr_t)(out_stride * 2)) % 16 != 0)
+    return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "row dequant needs 16-byte aligned rows");
+  if (int rc = require_sm100()) return rc;
+  return launch_dequant_rows(kv, num_slots, slots, n, out, out_stride, method,
+                             static_cast<cudaStream_t>(stream));
+}
+
 int fp8mla_convert_req_index(const int32_t* req_id, const int32_t* block_table,
                              int64_t bt_stride, int64_t max_blocks, const int32_t* token_idx,
                              int64_t ti_stride, int64_t T, int64_t topk, int64_t block_size,

@@ -170,6 +170,29 @@ __device__ __forceinline__ void dequant4_hw(uint32_t w, float s, uint32_t& lo, u
   hi = pack_bf16x2(f23.x * s, f23.y * s);
 }
 
+// dequant4_hw with the two products of each pair in one packed fp32 multiply
+// (mul.rn.f32x2: each lane is an ordinary round-to-nearest fp32 product, so the
+// bits equal dequant4_hw's); fewer issue slots for load warps that are
+// instruction-bound.
+__device__ __forceinline__ void dequant4_hw_x2(uint32_t w, float s, uint32_t& lo, uint32_t& hi) {
+  uint32_t h01, h23;
+  asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n"
+      " cvt.rn.f16x2.e4m3x2 %0, l;\n cvt.rn.f16x2.e4m3x2 %1, h;\n}\n"
+      : "=r"(h01), "=r"(h23)
+      : "r"(w));
+  float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+  float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+  const float2 s2 = make_float2(s, s);
+  asm("mul.rn.f32x2 %0, %0, %1;\n"
+      : "+l"(reinterpret_cast<uint64_t&>(f01))
+      : "l"(reinterpret_cast<const uint64_t&>(s2)));
+  asm("mul.rn.f32x2 %0, %0, %1;\n"
+      : "+l"(reinterpret_cast<uint64_t&>(f23))
+      : "l"(reinterpret_cast<const uint64_t&>(s2)));
+  lo = pack_bf16x2(f01.x, f01.y);
+  hi = pack_bf16x2(f23.x, f23.y);
+}
+
 // Tile scale preparation for dequant4_bf16.
 __device__ __forceinline__ void prep_scale(float s, float& scale_x, bool& fused) {
   float sx = s * 1.329227995784915872903807060280344576e36f;  // * 2^120

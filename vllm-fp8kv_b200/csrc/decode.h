@@ -66,6 +66,8 @@ bool decode_tc_supported(const DecodeArgs& a);
 
 int launch_dequant(const uint8_t* in, int64_t n, void* out, int out_dtype, int method,
                    cudaStream_t st);
+int launch_dequant_rows(const uint8_t* kv, int64_t num_slots, const int32_t* slots, int64_t n,
+                        uint16_t* out, int64_t out_stride, int method, cudaStream_t st);
 int launch_ds_mla_write(const uint16_t* kv_c, int64_t kv_c_stride, const uint16_t* k_pe,
                         int64_t k_pe_stride, const int64_t* slot_mapping, int64_t N,
                         uint8_t* cache, int64_t num_slots, cudaStream_t st);

@@ -263,10 +263,10 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
                      : (i >> 1) == 2 ? __uint_as_float(P.sc.z)
                                      : __uint_as_float(P.sc.w);
     uint4 o0, o1;
-    dequant4_hw(P.f[i].x, sc, o0.x, o0.y);
-    dequant4_hw(P.f[i].y, sc, o0.z, o0.w);
-    dequant4_hw(P.f[i].z, sc, o1.x, o1.y);
-    dequant4_hw(P.f[i].w, sc, o1.z, o1.w);
+    dequant4_hw_x2(P.f[i].x, sc, o0.x, o0.y);
+    dequant4_hw_x2(P.f[i].y, sc, o0.z, o0.w);
+    dequant4_hw_x2(P.f[i].z, sc, o1.x, o1.y);
+    dequant4_hw_x2(P.f[i].w, sc, o1.z, o1.w);
     *reinterpret_cast<uint4*>(blk + swz(row, 2 * p)) = o0;
     *reinterpret_cast<uint4*>(blk + swz(row, 2 * p + 1)) = o1;
   };

@@ -1,5 +1,6 @@
 // unit_kernels.cu -- the small kernels around the decode:
 //   * e4m3fn byte decode (unit test of the fused decode's dequant),
+//   * gather + dequant of fp8_ds_mla rows with the decode's own device dequant,
 //   * the fp8_ds_mla cache writer,
 //   * the block-table -> flat slot index converter.
 // All are HBM-bound integer/byte work; grids are sized in multiples of the SM
@@ -44,6 +45,58 @@ __global__ void dequant_e4m3_kernel(const uint8_t* __restrict__ in, int64_t n,
       static_cast<__half*>(out)[i] = __float2half_rn(v);
     } else {
       static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// ============================================================= row gather + dequant
+// The decode kernels' in-register dequant, run on its own: rows gathered by
+// slot (int64 byte offsets; slot -1 or >= num_slots gives a zero row), latent
+// bf16(e4m3 * tile scale) through the same device function the decode uses
+// (method 0: dequant4_hw, the general kernel's; method 1: dequant4_hw_x2, the
+// tcgen05 kernel's), rope copied raw.  Reference: the IS_FP8 gather and
+// dequant of vllm_fp8kv/fp8_ds_mla_sparse_decode.py:136-168 (exact fp32 decode,
+// times the fp32 tile scale, rounded to the query dtype bf16).
+// One thread per 16-byte chunk: chunks 0..31 of a row are latent (16 values,
+// tile c/8), chunks 32..39 the rope.
+template <int kMethod>
+__global__ void dequant_rows_kernel(const uint8_t* __restrict__ kv, int64_t num_slots,
+                                    const int32_t* __restrict__ slots, int64_t n,
+                                    uint16_t* __restrict__ out, int64_t out_stride) {
+  constexpr int kChunks = kNope / 16 + kRope * 2 / 16;  // 32 + 8
+  const int64_t total = n * kChunks;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / kChunks;
+    const int c = (int)(i - r * kChunks);
+    const int32_t slot = slots[r];
+    const bool valid = slot >= 0 && (int64_t)slot < num_slots;
+    const uint8_t* row = kv + (valid ? (int64_t)slot : 0) * (int64_t)kRowBytes;
+    uint16_t* dst = out + r * out_stride;
+    if (c < kNope / 16) {
+      uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
+      if (valid) {
+        const uint4 w = *reinterpret_cast<const uint4*>(row + 16 * c);
+        const float sc = reinterpret_cast<const float*>(row + kScaleOff)[c / 8];
+        if (kMethod == 0) {
+          dequant4_hw(w.x, sc, o0.x, o0.y);
+          dequant4_hw(w.y, sc, o0.z, o0.w);
+          dequant4_hw(w.z, sc, o1.x, o1.y);
+          dequant4_hw(w.w, sc, o1.z, o1.w);
+        } else {
+          dequant4_hw_x2(w.x, sc, o0.x, o0.y);
+          dequant4_hw_x2(w.y, sc, o0.z, o0.w);
+          dequant4_hw_x2(w.z, sc, o1.x, o1.y);
+          dequant4_hw_x2(w.w, sc, o1.z, o1.w);
+        }
+      }
+      reinterpret_cast<uint4*>(dst + 16 * c)[0] = o0;
+      reinterpret_cast<uint4*>(dst + 16 * c)[1] = o1;
+    } else {
+      const int rc = c - kNope / 16;
+      const uint4 v = valid ? *reinterpret_cast<const uint4*>(row + kRopeOff + 16 * rc)
+                            : make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(dst + kNope + 8 * rc) = v;
     }
   }
 }
@@ -193,6 +246,18 @@ int launch_dequant(const uint8_t* in, int64_t n, void* out, int out_dtype, int m
       dequant_e4m3_kernel<FP8MLA_DTYPE_F32><<<grid, block, 0, st>>>(in, n, out, method);
   }
   return check_cuda(cudaGetLastError(), "dequant_e4m3_kernel launch");
+}
+
+int launch_dequant_rows(const uint8_t* kv, int64_t num_slots, const int32_t* slots, int64_t n,
+                        uint16_t* out, int64_t out_stride, int method, cudaStream_t st) {
+  if (n == 0) return FP8MLA_OK;
+  const int block = 256;
+  const int grid = grid_for(n * 40, block);
+  if (method == 0)
+    dequant_rows_kernel<0><<<grid, block, 0, st>>>(kv, num_slots, slots, n, out, out_stride);
+  else
+    dequant_rows_kernel<1><<<grid, block, 0, st>>>(kv, num_slots, slots, n, out, out_stride);
+  return check_cuda(cudaGetLastError(), "dequant_rows_kernel launch");
 }
 
 int launch_ds_mla_write(const uint16_t* kv_c, int64_t kv_c_stride, const uint16_t* k_pe,

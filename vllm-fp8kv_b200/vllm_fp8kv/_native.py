@@ -51,6 +51,7 @@ SIGNATURES = {
         _P, _I64, _I64, _P, _I64, _I32, _P]),
     "fp8mla_ds_mla_write": (_I32, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P]),
     "fp8mla_dequant_e4m3": (_I32, [_P, _I64, _P, _I32, _I32, _P]),
+    "fp8mla_ds_mla_dequant_rows": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I32, _P]),
     "fp8mla_convert_req_index": (_I32, [_P, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64,
                                         _P, _I64, _P]),
 }

@@ -10,7 +10,11 @@ Same surface as the reference module (vllm_fp8kv/fp8_dequant.py:47-113):
   the fused decode uses (byte magnitude placed in fp32 bits [26:20] gives the
   value times 2^-120, rescaled exactly);
 * ``dequant_triton_launch`` -- the reference's test driver name, kept for
-  callers: returns (bit-math fp16, table-dtype decode) computed on device.
+  callers: returns (bit-math fp16, table-dtype decode) computed on device;
+* ``dequant_ds_mla_rows`` -- gather fp8_ds_mla rows by slot and dequantize
+  them with the decode kernels' own device code (bf16(e4m3 * tile scale),
+  raw rope), the IS_FP8 gather of the reference decode kernel
+  (vllm_fp8kv/fp8_ds_mla_sparse_decode.py:136-168) run on its own.
 
 All of them are exact for every finite byte; 0x7F / 0xFF decode to NaN (the
 payload differs between torch's CPU and CUDA casts, so compare NaN-ness).
@@ -61,3 +65,26 @@ def dequant_device(u8: torch.Tensor, dtype: torch.dtype = torch.float16,
 def dequant_triton_launch(u8: torch.Tensor, lut: torch.Tensor):
     """Reference-compatible driver: (bit-math decode as fp16, decode in lut.dtype)."""
     return dequant_device(u8, torch.float16, method=1), dequant_device(u8, lut.dtype, method=0)
+
+
+def dequant_ds_mla_rows(kv_cache: torch.Tensor, slots: torch.Tensor, method: int = 1) -> torch.Tensor:
+    """bf16 [n, 576] rows: bf16(float(e4m3) * fp32 tile scale) | raw rope.
+
+    ``kv_cache`` is any uint8 / float8 view of the [num_slots, 656] fp8_ds_mla
+    pool (paged shapes are flattened); ``slots`` int32 [n], entries < 0 or
+    >= num_slots give zero rows.  method 0 runs the general decode kernel's
+    dequant, 1 the tcgen05 kernel's; both must equal torch's
+    ``float8_e4m3fn -> float32 * scale -> bfloat16``.
+    """
+    assert method in (0, 1)
+    assert slots.dtype == torch.int32 and slots.dim() == 1
+    N.require_cuda(kv_cache)
+    kv = kv_cache.view(torch.uint8) if kv_cache.dtype != torch.uint8 else kv_cache
+    assert kv.is_contiguous() and kv.numel() % 656 == 0, "fp8_ds_mla pool must be contiguous"
+    num_slots = kv.numel() // 656
+    sl = slots.contiguous()
+    out = torch.empty((sl.numel(), 576), dtype=torch.bfloat16, device=kv.device)
+    rc = N.lib().fp8mla_ds_mla_dequant_rows(kv.data_ptr(), num_slots, sl.data_ptr(), sl.numel(),
+                                            out.data_ptr(), 576, method, N.stream_ptr(kv.device))
+    N.check(rc, "fp8mla_ds_mla_dequant_rows")
+    return out
