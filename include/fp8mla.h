@@ -86,7 +86,7 @@ FP8MLA_API int64_t fp8mla_decode_workspace_bytes(int64_t T, int64_t H, int64_t G
 
 /*
  * Name of the decode kernel fp8mla_sparse_decode dispatches for this shape
- * ("decode_tc_kernel" for 128 heads per kv group with bf16 q, else
+ * ("decode_tc2_kernel" for 128 heads per kv group with bf16 q, else
  * "decode_mma_kernel"; "+merge_splits_kernel" is appended when the call splits
  * the top-k axis).  Host-only; introspection for benchmarks and profiling.
  * No reference counterpart (the reference has one Triton kernel per path).

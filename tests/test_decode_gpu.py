@@ -324,8 +324,8 @@ def test_no_on_chip_wait_timed_out(cuda_device):
 def test_h128_bf16_dispatches_to_tcgen05(cuda_device):
     from vllm_fp8kv.fp8_ds_mla_sparse_decode import decode_kernel_name
 
-    assert decode_kernel_name(64, 128, 1, 2048) == "decode_tc_kernel"
-    assert decode_kernel_name(64, 256, 2, 2048) == "decode_tc_kernel"
+    assert decode_kernel_name(64, 128, 1, 2048) == "decode_tc2_kernel"
+    assert decode_kernel_name(64, 256, 2, 2048) == "decode_tc2_kernel"
     assert decode_kernel_name(64, 128, 1, 2048, torch.float32) == "decode_mma_kernel"
     assert decode_kernel_name(256, 16, 1, 2048, torch.bfloat16, 8) == \
         "decode_mma_kernel+merge_splits_kernel"

@@ -138,8 +138,8 @@ const char* fp8mla_decode_kernel_name(int64_t T, int64_t H, int64_t G, int64_t t
   a.hpg = (int)(H / G);
   a.num_splits = S < 1 ? 1 : S;
   const bool tc = decode_tc_supported(a);
-  if (a.num_splits > 1) return tc ? "decode_tc_kernel+merge_splits_kernel" : "decode_mma_kernel+merge_splits_kernel";
-  return tc ? "decode_tc_kernel" : "decode_mma_kernel";
+  if (a.num_splits > 1) return tc ? "decode_tc2_kernel+merge_splits_kernel" : "decode_mma_kernel+merge_splits_kernel";
+  return tc ? "decode_tc2_kernel" : "decode_mma_kernel";
 }
 
 }  // extern "C"
@@ -232,7 +232,7 @@ int decode_impl(const void* q, int q_dtype, int64_t T, int64_t H, int64_t q_stri
     a.block_size = (int)paged->block_size;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (decode_tc_supported(a)) return launch_decode_tc(a, st);
+  if (decode_tc_supported(a)) return launch_decode_tc2(a, st);
   return launch_decode_mma(a, st);
 }
 

@@ -61,8 +61,8 @@ __device__ __forceinline__ int32_t request_of(const DecodeArgs& a, int64_t t) {
 int launch_decode_mma(const DecodeArgs& a, cudaStream_t st);
 int launch_merge_splits(const DecodeArgs& a, cudaStream_t st);
 int read_device_status(unsigned int* status, bool reset, cudaStream_t st);
-int launch_decode_tc(const DecodeArgs& a, cudaStream_t st);
 bool decode_tc_supported(const DecodeArgs& a);
+int launch_decode_tc2(const DecodeArgs& a, cudaStream_t st);
 
 int launch_dequant(const uint8_t* in, int64_t n, void* out, int out_dtype, int method,
                    cudaStream_t st);
