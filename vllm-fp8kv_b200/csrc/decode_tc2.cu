@@ -47,8 +47,8 @@
 //               registers hold the next tile's rows while this tile is
 //               written, slots are read two tiles ahead.
 // Barriers that gate the issuing thread (tile data, P, Q) live in the even
-// CTA and count arrivals of both CTAs (one per warp, release at cluster
-// scope); completion of pair MMAs is signalled to both CTAs by a multicast
+// CTA and count arrivals of both CTAs (one per warp; the odd CTA's by remote
+// arrive); completion of pair MMAs is signalled to both CTAs by a multicast
 // commit.  Every wait is bounded (g_device_status records a timeout, the roles
 // drain what they issued and both CTAs free their tensor memory).
 //

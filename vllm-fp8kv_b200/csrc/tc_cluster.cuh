@@ -9,12 +9,16 @@
 namespace fp8mla {
 namespace tc {
 
-// Wait with cluster-scope acquire, for barriers the peer CTA arrives on (its
-// prior shared::cluster stores become visible to this thread).
+// Waits and remote arrivals use the default (CTA-scope) acquire / release,
+// the forms CUTLASS's 2-SM kernels use between the CTAs of a pair.  A release
+// at cluster scope first waits for every load the thread has in flight (about
+// 4.5 K cycles with a tile of row loads outstanding, 320 with none, measured);
+// the data it would order lives in the arriving CTA's own shared memory and
+// is read by that SM's tensor core, after the writer's proxy fence.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
       " selp.b32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
@@ -52,9 +56,9 @@ __device__ __forceinline__ uint32_t mapa(uint32_t local, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(local), "r"(rank));
   return r;
 }
-// release-at-cluster-scope arrive on a barrier in another CTA of the cluster
+// arrive on a barrier in another CTA of the cluster
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t raddr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(raddr)
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];\n" ::"r"(raddr)
                : "memory");
 }
 __device__ __forceinline__ void cluster_sync_all() {
@@ -67,7 +71,7 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   return r;
 }
 // Arrive on the barrier at shared::cta offset `bar` of CTA `rank` (this CTA
-// included) with release semantics at cluster scope.
+// included).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar, uint32_t rank) {
   mbar_arrive_remote(mapa(bar, rank));
 }
