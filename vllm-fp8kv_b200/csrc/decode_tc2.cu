@@ -71,11 +71,16 @@ constexpr int kHeads = 128;        // per kv group = per pair
 constexpr int kN = 64;             // tokens per tile
 constexpr int kOwn = kN / 2;       // tokens per tile whose whole row a CTA gathers
 constexpr int kKSteps = 36;        // 576 / 16
+// One extra k-step carries the mask: K column 576 is 0 for a live token and
+// -inf for a masked one, Q column 576 is 1 (the rest of the k-step is 0), so
+// the MMA itself makes S = -inf for masked tokens and the softmax needs no
+// validity bits.
+constexpr int kMaskBlock = 9;      // K block / Q block index holding column 576
 constexpr int kQTmemSteps = 24;    // q dims [0,384) from tensor memory
-constexpr int kQSmemBlocks = 3;    // q dims [384,576)
+constexpr int kQSmemBlocks = 4;    // q dims [384,576) and the mask column
 constexpr int kQBlockBytes = 64 * 128;   // 64 rows (this CTA's heads)
 constexpr int kKBlockBytes = kOwn * 128;  // 4096: 32 own rows of a 64-dim block
-constexpr int kKStageBytes = 9 * kKBlockBytes;
+constexpr int kKStageBytes = 10 * kKBlockBytes;  // 9 data blocks + the mask block
 constexpr int kKStages = 2;
 constexpr int kVBlockBytes = kN * 128;    // 8192: 64 rows of a 64-dim block
 constexpr int kVStageBytes = 4 * kVBlockBytes;
@@ -100,11 +105,10 @@ struct Smem {
   uint8_t k[kKStages][kKStageBytes];
   uint8_t v[kVStages][kVStageBytes];
   uint8_t p[kPStages][kPStageBytes];
-  uint8_t vbits[kVStages][kLoadWarps];     // validity of rows 8w..8w+7 of a tile
   float pmax[2][128];                      // partial tile max, by tile parity
   float lsum[128];                         // partial row sums (epilogue)
   uint64_t tfull[kVStages];                // even CTA: tile j's rows in both CTAs
-  uint64_t kempty[kKStages], vempty[kVStages], vloc[kVStages];
+  uint64_t kempty[kKStages], vempty[kVStages];
   uint64_t sfull[2], pfull[kPStages], pempty[kPStages];
   uint64_t xch[2];                         // partial-max exchange, by tile parity
   uint64_t qready, ofull, drain;
@@ -136,7 +140,7 @@ struct Ctx {
   uint32_t rank;  // 0 = the CTA that issues the pair's MMAs
   uint32_t tmem;
   uint32_t sq, sk0, sv0, sp0;
-  uint32_t b_tfull, b_kempty, b_vempty, b_vloc, b_sfull, b_pfull, b_pempty;
+  uint32_t b_tfull, b_kempty, b_vempty, b_sfull, b_pfull, b_pempty;
   uint32_t b_xch, b_qready, b_ofull, b_drain;
 };
 
@@ -155,6 +159,9 @@ __device__ __forceinline__ void issue_qk(uint32_t tS, uint32_t tQ, uint64_t qdes
       mma_pair_ss(tS, adesc, bdesc, kIdescQK, 1u);
     }
   }
+  // the mask k-step: Q block 3 / K block 9, first 16 columns
+  mma_pair_ss(tS, qdesc0 + (uint64_t)((3 * kQBlockBytes) >> 4),
+              kdesc + (uint64_t)((kMaskBlock * kKBlockBytes) >> 4), kIdescQK, 1u);
 }
 
 __device__ void mma_role(const Ctx& c) {
@@ -225,9 +232,10 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
     const int pos = c.beg + jt * kN + row;
     return pos < c.end ? live_slot(a, c.req, c.idx_row[pos]) : -1;
   };
-  auto load = [&](int32_t sa, int32_t sb, Rows& R, bool& va) {
-    va = sa >= 0;
-    if (va) {
+  // vb: own row rowB is live (its mask column is 0, else -inf)
+  auto load = [&](int32_t sa, int32_t sb, Rows& R, bool& vb) {
+    vb = sb >= 0;
+    if (sa >= 0) {
       const uint8_t* src = a.kv + sa * (int64_t)kRowBytes;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -262,7 +270,7 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
   bool ok = true;
   int32_t nA = c.ntiles > 1 ? slot_at(1, rowA) : -1;
   int32_t nB = c.ntiles > 1 ? slot_at(1, kOwn * cr + rowB) : -1;
-  auto step = [&](int j, const Rows& cur, bool vcur, Rows& nxt, bool& vnxt) {
+  auto step = [&](int j, const Rows& cur, bool vownB, Rows& nxt, bool& vnxt) {
     if (!ok || j >= c.ntiles) return;
     const int32_t sa1 = nA, sb1 = nB;
     if (j + 2 < c.ntiles) {
@@ -293,7 +301,6 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
         *reinterpret_cast<uint4*>(kb + swz(r, 2 * pA + 1)) = o1;
       }
     }
-    const uint32_t vb = __ballot_sync(0xFFFFFFFFu, pA == 0 && vcur);  // bits 0..7 = rows 8lw..+7
     // part B -> K stage: the other two latent tiles and the rope of own row rowB
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -305,13 +312,14 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
       *reinterpret_cast<uint4*>(kb + swz(rowB, 2 * (qB & 3) + 1)) = o1;
     }
     *reinterpret_cast<uint4*>(kst + 8 * kKBlockBytes + swz(rowB, qB)) = cur.brope;
-    if (lane == 0) s.vbits[vs][lw] = (uint8_t)(vb & 0xFFu);
+    // mask column of own row rowB: bf16 0 (live) or -inf (masked); the other
+    // 15 columns of the k-step (chunk 1 and the rest of chunk 0) stay 0
+    if (qB < 2)
+      *reinterpret_cast<uint4*>(kst + kMaskBlock * kKBlockBytes + swz(rowB, qB)) =
+          make_uint4(qB == 0 && !vownB ? 0xFF80u : 0u, 0u, 0u, 0u);
     fence_proxy_async_smem();
     __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(c.b_vloc + 8 * vs);                 // validity bits, this CTA's softmax
-      mbar_arrive_cluster(c.b_tfull + 8 * vs, 0);     // the issuing CTA's tile barrier
-    }
+    if (lane == 0) mbar_arrive_cluster(c.b_tfull + 8 * vs, 0);  // the issuing CTA's tile barrier
   };
   Rows A, B;
   bool vA = false, vB = false;
@@ -353,7 +361,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   c.b_tfull = smem_u32(&s.tfull[0]);
   c.b_kempty = smem_u32(&s.kempty[0]);
   c.b_vempty = smem_u32(&s.vempty[0]);
-  c.b_vloc = smem_u32(&s.vloc[0]);
   c.b_sfull = smem_u32(&s.sfull[0]);
   c.b_pfull = smem_u32(&s.pfull[0]);
   c.b_pempty = smem_u32(&s.pempty[0]);
@@ -366,7 +373,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kVStages; ++i) {
       mbar_init(c.b_tfull + 8 * i, 2 * kLoadWarps);
       mbar_init(c.b_vempty + 8 * i, 1);
-      mbar_init(c.b_vloc + 8 * i, kLoadWarps);
     }
     for (int i = 0; i < kKStages; ++i) mbar_init(c.b_kempty + 8 * i, 1);
     for (int i = 0; i < 2; ++i) {
@@ -416,11 +422,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tmem_st32(trow + kColQ + c0, w);
       }
 #pragma unroll
-      for (int blk = 0; blk < kQSmemBlocks; ++blk)
+      for (int blk = 0; blk < kQSmemBlocks - 1; ++blk)
 #pragma unroll
         for (int cc = 4 * hh; cc < 4 * hh + 4; ++cc)
           *reinterpret_cast<uint4*>(s.q + blk * kQBlockBytes + swz(m, cc)) =
               qsrc[kQTmemSteps * 2 + blk * 8 + cc];
+      if (hh == 0) {  // mask k-step of Q: bf16 1.0 in column 576, zeros in 577..591
+        *reinterpret_cast<uint4*>(s.q + 3 * kQBlockBytes + swz(m, 0)) = make_uint4(0x3F80u, 0, 0, 0);
+        *reinterpret_cast<uint4*>(s.q + 3 * kQBlockBytes + swz(m, 1)) = make_uint4(0, 0, 0, 0);
+      }
       tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
@@ -431,19 +441,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < c.ntiles && ok; ++j) {
-      const int b = j & 1, vs = j % kVStages, ps = j % kPStages;
+      const int b = j & 1, ps = j % kPStages;
       ok = warp_wait_cluster(c.b_sfull + 8 * b, (j >> 1) & 1, 1);
-      if (ok) ok = warp_wait(c.b_vloc + 8 * vs, (j / kVStages) & 1, 2);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t vm = *reinterpret_cast<const uint32_t*>(&s.vbits[vs][4 * hh]);
       uint32_t sv[32];
       tmem_ld32(trow + kColS + kSBufCols * b, sv);
       tmem_wait_ld();
       float pm = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if ((vm >> i) & 1u) pm = fmaxf(pm, __uint_as_float(sv[i]) * a.scale_log2);
+      for (int i = 0; i < 32; ++i) pm = fmaxf(pm, __uint_as_float(sv[i]));  // masked: -inf
+      pm *= a.scale_log2;
       s.pmax[b][L] = pm;
       __syncwarp();
       if (lane == 0) mbar_arrive(c.b_xch + 8 * b);
@@ -478,19 +486,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t pk[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const float x0 = ((vm >> (2 * i)) & 1u) ? __uint_as_float(sv[2 * i]) * a.scale_log2 : -INFINITY;
-        const float x1 =
-            ((vm >> (2 * i + 1)) & 1u) ? __uint_as_float(sv[2 * i + 1]) * a.scale_log2 : -INFINITY;
-        const float p0 = ex2_approx(x0 - mref), p1 = ex2_approx(x1 - mref);
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * i]), a.scale_log2, -mref));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * i + 1]), a.scale_log2, -mref));
         l += p0 + p1;
         pk[i] = pack_bf16x2(p0, p1);
       }
-      // P stage ps was last read by PV(j-2)
-      if (j >= kPStages) {
-        const int jp = j - kPStages;
-        ok = warp_wait_cluster(c.b_pempty + 8 * ps, (jp / kPStages) & 1, 13);
-        if (!ok) break;
-      }
+      // P stage ps was last read by PV(j-2), which was issued before QK(j): its
+      // completion is implied by sfull(j) (a commit arrives once every earlier
+      // MMA of the issuing thread has completed)
       uint8_t* prow = s.p[ps];
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4)
