@@ -3,7 +3,8 @@
 //
 // The pair splits the heads, not the output dims: CTA c owns heads
 // [64c, 64c+64) and its TMEM holds their S and O.  One MMA spans both SMs:
-//   S = Q K^T   M=128 heads (64 per CTA), N=64 tokens, K=576 (36 k-steps)
+//   S = Q K^T   M=128 heads (64 per CTA), N=64 tokens, K=576 (36 k-steps) plus
+//               one mask k-step (S = -inf for masked tokens)
 //               B is split by N: CTA c supplies the rows of tokens [32c, 32c+32)
 //               of the 64-token tile (its "own" tokens), all 576 dims.
 //   O += P V    M=128 heads, N=256 dims (two MMAs for the 512), K=64 tokens
@@ -27,9 +28,10 @@
 //   [256,320)  2 S buffers x 32 fp32 columns
 //   [320,512)  Q dims [0,384) as the A operand of the TMEM-A MMA (24 k-steps,
 //              8 bf16x2 columns each; lanes L and L^64 hold the same head)
-// Shared memory (208 KB):
-//   q   Q dims [384,576): 3 x 64-dim swizzled blocks (64 rows)
-//   k   2 stages: own tokens x 576 dims, 9 x 64-dim blocks of 32 rows (QK B)
+// Shared memory (224 KB):
+//   q   Q dims [384,576) and the mask column: 4 x 64-dim swizzled blocks (64 rows)
+//   k   2 stages: own tokens x 576 dims + mask column, 10 x 64-dim blocks of 32
+//       rows (QK B)
 //   v   3 stages: 64 tokens x PV-half dims, 4 x 64-dim blocks of 64 rows,
 //       read MN-major as the PV B operand
 //   p   2 stages: P (bf16) of this CTA's 64 heads x 64 tokens (PV A operand)
