@@ -24,7 +24,8 @@ struct DecodeArgs {
   int64_t lse_st;
   int num_splits;
   int split_len;     // top-k entries per split (last split may be shorter)
-  float* ws_o;       // [T][H][S][512] fp32 normalised split outputs
+  float* ws_o;       // [T][H][S][512] normalised split outputs: bf16 (as uint16)
+                     // when the output is bf16, fp32 when it is fp32
   float* ws_lse;     // [T][H][S] natural-log split LSE
   // Optional block-table indirection (fp8mla_sparse_decode_paged): when
   // block_table is set, idx holds request-local token positions and the slot

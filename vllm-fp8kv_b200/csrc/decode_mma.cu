@@ -14,8 +14,9 @@
 //   dequant  one warp per row: e4m3 * tile scale -> bf16 (hardware e4m3x2 ->
 //            f16x2, exact fp32 product then RNE, as the reference:
 //            decode.py:152-164);
-//   QK^T     warp w: tokens 8(w % (BN/8))..+7 over a 1/(64/BN) share of
-//            d = 576 (m16n8k16 k-steps); the shares meet in shared memory;
+//   QK^T     warp w: 16 tokens (two n8 tiles per loaded Q fragment) over a
+//            1/(8/(BN/16)) share of d = 576 (m16n8k16 k-steps); the shares
+//            meet in shared memory;
 //   softmax  16 threads per head, BN/16 tokens each (exp2 form; a still -inf
 //            running max is replaced by 0 so a fully masked chunk contributes
 //            nothing: decode.py:178-197);
@@ -36,13 +37,17 @@ constexpr int kKStride = 584;   // bf16 per sQ / sK row: 576 + 8 (1168 B = 73 x 
 
 template <int BN>  // tokens per chunk: 32 or 64
 struct Cfg {
-  static constexpr int kParts = 64 / BN;              // d shares per token tile
-  static constexpr int kPartSteps = kDqk / 16 / kParts;  // k-steps per share
+  // QK^T: a warp owns 16 tokens (two n8 tiles share each Q fragment it loads)
+  // and a 1/kParts share of d = 576; the shares meet in shared memory.
+  static constexpr int kTokGroups = BN / 16;
+  static constexpr int kParts = kThreads / 32 / kTokGroups;  // d shares
+  static constexpr int kPartSteps = kDqk / 16 / kParts;      // k-steps per share
   static constexpr int kPStride = BN + 8;
   static constexpr int kSStride = BN + 1;
   static constexpr int kRowThreads = kThreads / BN;   // gather threads per row
   static constexpr int kMinBlocks = BN == 32 ? 2 : 1;
-  static_assert(kThreads / 32 == (BN / 8) * kParts, "one warp per (token tile, d share)");
+  static_assert(kThreads / 32 == kTokGroups * kParts && kDqk / 16 % kParts == 0,
+                "one warp per (16-token group, d share)");
 };
 
 template <int BN>
@@ -171,27 +176,32 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::kMinBlocks)
     if (c + 2 < nchunks) issue_gather(s, buf, a, idx_row, req, beg + (c + 2) * kBN, end);
     cp_async_commit();
 
-    // ---- partial S = Q K^T: tokens 8(w % (BN/8))..+7, d share w / (BN/8)
+    // ---- partial S = Q K^T: tokens 16(w % groups)..+15, d share w / groups
     {
-      const int n0 = (warp % (kBN / 8)) * 8, k0 = (warp / (kBN / 8)) * C::kPartSteps;
-      float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int n0 = (warp % C::kTokGroups) * 16, k0 = (warp / C::kTokGroups) * C::kPartSteps;
+      float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      // ldmatrix rows: lane l -> Q row l & 15, column half l >> 4; K token
+      // n0 + 8 (l >> 4) + (l & 7), column half (l >> 3) & 1
+      const uint32_t qa0 = q_base + (((lane & 15) * kKStride + (lane >> 4) * 8) << 1);
+      const uint32_t kb0 =
+          k_base + (((n0 + ((lane >> 4) << 3) + (lane & 7)) * kKStride + ((lane >> 3) & 1) * 8) << 1);
 #pragma unroll 3
-      for (int kk = k0; kk < k0 + C::kPartSteps; kk += 2) {
-        uint32_t a0, a1, a2, a3, a4, a5, a6, a7, b0, b1, b2, b3;
-        const uint32_t qa = q_base + (((lane & 15) * kKStride + kk * 16 + (lane >> 4) * 8) << 1);
-        ldmatrix_x4(qa, a0, a1, a2, a3);
-        ldmatrix_x4(qa + 32, a4, a5, a6, a7);
-        const uint32_t kb = k_base + (((n0 + (lane & 7)) * kKStride + kk * 16 + (lane >> 3) * 8) << 1);
-        ldmatrix_x4(kb, b0, b1, b2, b3);
-        mma_bf16_16816(sacc, a0, a1, a2, a3, b0, b1);
-        mma_bf16_16816(sacc, a4, a5, a6, a7, b2, b3);
+      for (int kk = k0; kk < k0 + C::kPartSteps; ++kk) {
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+        ldmatrix_x4(qa0 + kk * 32, a0, a1, a2, a3);
+        ldmatrix_x4(kb0 + kk * 32, b0, b1, b2, b3);
+        mma_bf16_16816(sacc[0], a0, a1, a2, a3, b0, b1);
+        mma_bf16_16816(sacc[1], a0, a1, a2, a3, b2, b3);
       }
-      float* sp = s.sp[warp / (kBN / 8)];
-      const int col = n0 + q4 * 2;
-      sp[g * kSStride + col] = sacc[0];
-      sp[g * kSStride + col + 1] = sacc[1];
-      sp[(g + 8) * kSStride + col] = sacc[2];
-      sp[(g + 8) * kSStride + col + 1] = sacc[3];
+      float* sp = s.sp[warp / C::kTokGroups];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int col = n0 + 8 * t + q4 * 2;
+        sp[g * kSStride + col] = sacc[t][0];
+        sp[g * kSStride + col + 1] = sacc[t][1];
+        sp[(g + 8) * kSStride + col] = sacc[t][2];
+        sp[(g + 8) * kSStride + col + 1] = sacc[t][3];
+      }
     }
     __syncthreads();
 
@@ -285,11 +295,19 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::kMinBlocks)
       if (a.lse != nullptr && warp == 0 && q4 == 0) a.lse[t * a.lse_st + h] = lse_v;
     } else {
       const int64_t base = ((t * a.H + h) * a.num_splits + split);
-      float* o = a.ws_o + base * kNope + d0;
+      if constexpr (sizeof(OT) == 2) {  // bf16 output: bf16 partials (half the traffic)
+        uint16_t* o = reinterpret_cast<uint16_t*>(a.ws_o) + base * kNope + d0;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
-        *reinterpret_cast<float2*>(o + nt * 8) =
-            make_float2(acc[nt][half * 2] * inv, acc[nt][half * 2 + 1] * inv);
+        for (int nt = 0; nt < 8; ++nt)
+          *reinterpret_cast<uint32_t*>(o + nt * 8) =
+              pack_bf16x2(acc[nt][half * 2] * inv, acc[nt][half * 2 + 1] * inv);
+      } else {
+        float* o = a.ws_o + base * kNope + d0;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+          *reinterpret_cast<float2*>(o + nt * 8) =
+              make_float2(acc[nt][half * 2] * inv, acc[nt][half * 2 + 1] * inv);
+      }
       if (warp == 0 && q4 == 0) a.ws_lse[base] = lse_v;
     }
   }
@@ -297,6 +315,8 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::kMinBlocks)
 
 // LSE merge of split partials: out = sum_s w_s o_s / sum_s w_s with
 // w_s = exp(lse_s - max lse); an all-empty row gives zeros and LSE -inf.
+// Partials are bf16 for a bf16 output (each is normalised, so bf16 keeps its
+// relative precision; the sum is fp32) and fp32 for an fp32 output.
 // Reference: tests/fixtures/triton_mla_sparse_kernel_pr47629.py:331-403.
 template <typename OT>
 __global__ void __launch_bounds__(128) merge_splits_kernel(const DecodeArgs a) {
@@ -313,7 +333,15 @@ __global__ void __launch_bounds__(128) merge_splits_kernel(const DecodeArgs a) {
     for (int i = 0; i < S; ++i) {
       const float w = expf(lse_s[i] - m);
       denom += w;
-      const float4 o = *reinterpret_cast<const float4*>(a.ws_o + (th * S + i) * kNope + d);
+      float4 o;
+      if constexpr (sizeof(OT) == 2) {
+        const uint2 p = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(a.ws_o) +
+                                                        (th * S + i) * kNope + d);
+        o = make_float4(__uint_as_float(p.x << 16), __uint_as_float(p.x & 0xFFFF0000u),
+                        __uint_as_float(p.y << 16), __uint_as_float(p.y & 0xFFFF0000u));
+      } else {
+        o = *reinterpret_cast<const float4*>(a.ws_o + (th * S + i) * kNope + d);
+      }
       accv.x += w * o.x;
       accv.y += w * o.y;
       accv.z += w * o.z;

@@ -541,13 +541,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
         }
       } else {
-        float4* dst = reinterpret_cast<float4*>(
-            a.ws_o + ((t * a.H + hh_glob) * a.num_splits + split) * kNope + d);
+        // bf16 partials (the output is bf16), merged in fp32 by merge_splits_kernel
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.ws_o) +
+                                              ((t * a.H + hh_glob) * a.num_splits + split) * kNope + d);
 #pragma unroll
-        for (int v = 0; v < 8; ++v)
-          dst[v] = make_float4(__uint_as_float(o[4 * v]) * inv, __uint_as_float(o[4 * v + 1]) * inv,
-                               __uint_as_float(o[4 * v + 2]) * inv,
-                               __uint_as_float(o[4 * v + 3]) * inv);
+        for (int v = 0; v < 4; ++v) {
+          uint32_t w[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            w[u] = pack_bf16x2(__uint_as_float(o[8 * v + 2 * u]) * inv,
+                               __uint_as_float(o[8 * v + 2 * u + 1]) * inv);
+          dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
       }
     }
     if (hh == 0) {
