@@ -86,7 +86,7 @@ FP8MLA_API int64_t fp8mla_decode_workspace_bytes(int64_t T, int64_t H, int64_t G
 
 /*
  * Name of the decode kernel fp8mla_sparse_decode dispatches for this shape
- * ("decode_tc2_kernel" for 128 heads per kv group with bf16 q, else
+ * ("decode_tc2_kernel" for 128 or 64 heads per kv group with bf16 q, else
  * "decode_mma_kernel"; "+merge_splits_kernel" is appended when the call splits
  * the top-k axis).  Host-only; introspection for benchmarks and profiling.
  * No reference counterpart (the reference has one Triton kernel per path).
@@ -114,8 +114,13 @@ FP8MLA_API const char* fp8mla_decode_kernel_name(int64_t T, int64_t H, int64_t G
  *   out      [T, H, 512]   same dtype as q.
  *   lse      [T, H] fp32 natural-log LSE, or NULL.  -inf for a row that
  *                          selected nothing (its out row is all zeros).
- *   num_splits  0 = fp8mla_choose_num_splits(); otherwise 1..64 splits of the
- *               top-k axis merged by LSE.  Splits > 1 need `workspace`.
+ *   num_splits  0 = the library's choice: fp8mla_choose_num_splits() (the
+ *               upstream table), except that for the paired tcgen05 kernel (bf16
+ *               q, 64 or 128 heads per group) a table answer of 1 is raised to
+ *               the largest power of two that keeps T*G*splits CTA pairs within
+ *               one wave of SM pairs with at least 256 top-k entries per split;
+ *               otherwise 1..64 splits of the top-k axis merged by LSE.  Splits
+ *               > 1 need `workspace` (fp8mla_decode_workspace_bytes sizes it).
  *
  * Returns FP8MLA_ERR_INVALID_ARGUMENT for shape/stride/alignment violations.
  */

@@ -326,6 +326,10 @@ def test_h128_bf16_dispatches_to_tcgen05(cuda_device):
 
     assert decode_kernel_name(64, 128, 1, 2048) == "decode_tc2_kernel"
     assert decode_kernel_name(64, 256, 2, 2048) == "decode_tc2_kernel"
+    # 64 heads per group run on the pair kernel too (the odd CTA's rows are
+    # padding); 32 tokens x 1 group would fill 32 of 74 SM pairs, so the
+    # automatic split count doubles to 2
+    assert decode_kernel_name(32, 64, 1, 2048) == "decode_tc2_kernel+merge_splits_kernel"
     assert decode_kernel_name(64, 128, 1, 2048, torch.float32) == "decode_mma_kernel"
     assert decode_kernel_name(256, 16, 1, 2048, torch.bfloat16, 8) == \
         "decode_mma_kernel+merge_splits_kernel"

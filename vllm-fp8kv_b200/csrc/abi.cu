@@ -77,6 +77,21 @@ int pick_splits(int64_t T, int64_t H, int64_t G, int64_t topk, int sm_count) {
   return (int)(n < 1 ? 1 : n);
 }
 
+// Split count of a call with num_splits = 0.  The upstream table
+// (pick_splits) for the general kernel; for the paired tcgen05 kernel (bf16 q,
+// 64 or 128 heads per group), when that table gives one split and the pairs
+// would leave SMs idle, the largest power of two that keeps T*G*S pairs within
+// one wave of SM pairs and at least 4 tiles (256 entries) per split.
+int auto_splits(int64_t T, int64_t H, int64_t G, int64_t topk, bool pair_kernel, int sm_count) {
+  int S = pick_splits(T, H, G, topk, sm_count);
+  if (!pair_kernel || S != 1) return S;
+  const int64_t pairs = T * G, wave = sm_count / 2;
+  int64_t s = 1;
+  while (pairs * (s * 2) <= wave && topk % (s * 2) == 0 && topk / (s * 2) >= 256) s *= 2;
+  return (int)s;
+}
+bool pair_heads(int64_t H, int64_t G) { return G > 0 && (H / G == 128 || H / G == 64); }
+
 int64_t ws_bytes(int64_t T, int64_t H, int S) {
   if (S <= 1) return 0;
   const int64_t o = T * H * S * kNope * 4;
@@ -117,7 +132,8 @@ int64_t fp8mla_decode_workspace_bytes(int64_t T, int64_t H, int64_t G, int64_t t
                                       int num_splits) {
   if (num_splits <= 0) {
     if (G <= 0 || H <= 0 || H % G != 0) return 0;
-    num_splits = pick_splits(T, H, G, topk, device_sm_count());
+    // sized for the paired kernel's choice, an upper bound of the general one
+    num_splits = auto_splits(T, H, G, topk, pair_heads(H, G), device_sm_count());
   }
   if (num_splits > 64) num_splits = 64;
   return ws_bytes(T, H, num_splits);
@@ -126,7 +142,9 @@ int64_t fp8mla_decode_workspace_bytes(int64_t T, int64_t H, int64_t G, int64_t t
 const char* fp8mla_decode_kernel_name(int64_t T, int64_t H, int64_t G, int64_t topk, int q_dtype,
                                       int num_splits) {
   if (G <= 0 || H <= 0 || H % G != 0) return "";
-  int S = num_splits > 0 ? num_splits : pick_splits(T, H, G, topk, device_sm_count());
+  int S = num_splits > 0 ? num_splits
+                         : auto_splits(T, H, G, topk, q_dtype == FP8MLA_DTYPE_BF16 && pair_heads(H, G),
+                                       device_sm_count());
   if (S > 64) S = 64;
   if (topk > 0 && S > topk) S = (int)topk;
   DecodeArgs a{};
@@ -184,7 +202,9 @@ int decode_impl(const void* q, int q_dtype, int64_t T, int64_t H, int64_t q_stri
   if (int rc = require_sm100()) return rc;
 
   int S = num_splits;
-  if (S <= 0) S = pick_splits(T, H, G, topk, device_sm_count());
+  if (S <= 0)
+    S = auto_splits(T, H, G, topk, q_dtype == FP8MLA_DTYPE_BF16 && pair_heads(H, G),
+                    device_sm_count());
   if (S > 64) S = 64;
   if (topk > 0 && S > topk) S = (int)topk;
   if (S < 1) S = 1;

@@ -346,7 +346,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int grp = (blockIdx.x >> 1) % a.G;
   const int split = blockIdx.y;
   const uint32_t rank = cluster_rank();  // == blockIdx.x & 1
-  const int head0 = grp * kHeads + 64 * (int)rank;
+  // 128 heads per group, or 64: then the odd CTA's rows are padding (zero Q,
+  // nothing stored) and the even CTA holds every head
+  const int head0 = grp * a.hpg + 64 * (int)rank;
+  const int nh = max(0, min(64, a.hpg - 64 * (int)rank));  // real heads of this CTA
 
   Ctx c;
   c.a = &a;
@@ -407,15 +410,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
     {
       // Q dims [0,384) -> TMEM (lane L and L^64 both hold head m), dims [384,576)
-      // -> swizzled smem (thread hh writes chunks [4hh, 4hh+4) of each block)
+      // -> swizzled smem (thread hh writes chunks [4hh, 4hh+4) of each block);
+      // padding rows are zero
+      const bool hv = m < nh;
       const uint4* qsrc = reinterpret_cast<const uint4*>(
-          static_cast<const uint16_t*>(a.q) + t * a.q_st + (int64_t)(head0 + m) * a.q_sh);
+          static_cast<const uint16_t*>(a.q) + t * a.q_st + (int64_t)(hv ? head0 + m : 0) * a.q_sh);
+      const uint4 z4 = make_uint4(0, 0, 0, 0);
 #pragma unroll
       for (int c0 = 0; c0 < kQTmemSteps * 8; c0 += 32) {
         uint32_t w[32];
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
-          const uint4 x = qsrc[c0 / 4 + v];
+          const uint4 x = hv ? qsrc[c0 / 4 + v] : z4;
           w[4 * v] = x.x;
           w[4 * v + 1] = x.y;
           w[4 * v + 2] = x.z;
@@ -428,7 +434,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int cc = 4 * hh; cc < 4 * hh + 4; ++cc)
           *reinterpret_cast<uint4*>(s.q + blk * kQBlockBytes + swz(m, cc)) =
-              qsrc[kQTmemSteps * 2 + blk * 8 + cc];
+              hv ? qsrc[kQTmemSteps * 2 + blk * 8 + cc] : z4;
       if (hh == 0) {  // mask k-step of Q: bf16 1.0 in column 576, zeros in 577..591
         *reinterpret_cast<uint4*>(s.q + 3 * kQBlockBytes + swz(m, 0)) = make_uint4(0x3F80u, 0, 0, 0);
         *reinterpret_cast<uint4*>(s.q + 3 * kQBlockBytes + swz(m, 1)) = make_uint4(0, 0, 0, 0);
@@ -528,6 +534,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       // column c of MMA hf: dim 256 hf + 128 hh + (c mod 128)
       const int d = 256 * (c0 >> 7) + 128 * hh + (c0 & 127);
+      if (m >= nh) continue;  // padding row (the TMEM load above is warp-collective)
       if (a.num_splits == 1) {
         uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + t * a.out_st +
                                               (int64_t)hh_glob * a.out_sh + d);
@@ -555,7 +562,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (hh == 0) {
+    if (hh == 0 && m < nh) {
       if (a.num_splits == 1) {
         if (a.lse != nullptr) a.lse[t * a.lse_st + hh_glob] = lse_v;
       } else {
@@ -584,7 +591,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }  // namespace tc2
 
 bool decode_tc_supported(const DecodeArgs& a) {
-  return a.q_dtype == FP8MLA_DTYPE_BF16 && a.hpg == tc2::kHeads && a.G >= 1;
+  return a.q_dtype == FP8MLA_DTYPE_BF16 && (a.hpg == tc2::kHeads || a.hpg == tc2::kHeads / 2) &&
+         a.G >= 1;
 }
 
 int launch_decode_tc2(const DecodeArgs& a, cudaStream_t st) {
