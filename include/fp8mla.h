@@ -223,8 +223,9 @@ FP8MLA_API int fp8mla_dequant_e4m3(const uint8_t* in, int64_t n, void* out,
  * (row stride out_stride elements, >= 576, 16-byte aligned):
  * out[r, d] = bf16(float(e4m3 latent[d]) * scale[d / 128]) for d < 512 and the
  * raw rope for d >= 512; slot < 0 or >= num_slots gives a zero row.  It runs
- * the decode kernels' own device dequant (method 0: the general kernel's,
- * 1: the tcgen05 kernel's) so that both can be checked bit for bit.
+ * the decode kernels' own device dequant (method 1: the packed-multiply form
+ * both decode kernels use; 0: the same arithmetic unpacked) so that it can be
+ * checked bit for bit.
  * Replaces the IS_FP8 gather + dequant inside `_fp8_ds_mla_sparse_decode_kernel`
  * (vllm_fp8kv/fp8_ds_mla_sparse_decode.py:136-168).
  */

@@ -65,14 +65,13 @@ static_assert(sizeof(Smem<64>) <= 227 * 1024, "shared memory budget");
 static_assert(offsetof(Smem<32>, raw) % 16 == 0 && offsetof(Smem<64>, raw) % 16 == 0,
               "cp.async destinations must be 16-B aligned");
 
+// Row r = threadIdx.x / kRowThreads of a chunk is gathered by kRowThreads
+// threads; `slot` is that row's live slot (-1: masked, no global read).
 template <int BN>
 __device__ __forceinline__ void issue_gather(Smem<BN>& s, int buf, const DecodeArgs& a,
-                                             const int32_t* idx_row, int32_t req, int pos0,
-                                             int end) {
+                                             int32_t slot) {
   constexpr int kRT = Cfg<BN>::kRowThreads;
   const int r = threadIdx.x / kRT, sub = threadIdx.x % kRT;
-  const int pos = pos0 + r;
-  const int64_t slot = pos < end ? live_slot(a, req, idx_row[pos]) : -1;
   const bool ok = slot >= 0;
   const uint8_t* src = a.kv + (ok ? slot : 0) * (int64_t)kRowBytes;
   const uint32_t dst = smem_u32(&s.raw[buf][r * kRowBytes]);
@@ -106,10 +105,20 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::kMinBlocks)
   const int32_t req = request_of(a, t);
 
   const int nchunks = end > beg ? (end - beg + kBN - 1) / kBN : 0;
-  if (nchunks > 0) issue_gather(s, 0, a, idx_row, req, beg, end);
+  // Index prefetch: a chunk's raw top-k entry is loaded two chunks before its
+  // gather and turned into a slot (block-table lookup included) one chunk
+  // before, so issuing a gather never waits for an index load.
+  const int grow = tid / C::kRowThreads;  // this thread's gather row
+  auto raw_at = [&](int ch) -> int32_t {
+    const int pos = beg + ch * kBN + grow;
+    return (ch < nchunks && pos < end) ? idx_row[pos] : -1;
+  };
+  if (nchunks > 0) issue_gather(s, 0, a, live_slot(a, req, raw_at(0)));
   cp_async_commit();
-  if (nchunks > 1) issue_gather(s, 1, a, idx_row, req, beg + kBN, end);
+  if (nchunks > 1) issue_gather(s, 1, a, live_slot(a, req, raw_at(1)));
   cp_async_commit();
+  int32_t slot_n = live_slot(a, req, raw_at(2));  // chunk c + 2
+  int32_t raw_n = raw_at(3);                      // chunk c + 3
 
   // ---- Q -> smem (bf16), zero rows for padded heads
   for (int e = tid; e < kBH * (kDqk / 8); e += kThreads) {
@@ -150,16 +159,18 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::kMinBlocks)
     cp_async_wait<1>();
     __syncthreads();
 
-    // ---- dequant raw[buf] -> k (bf16): warp per row, lane owns 16 bytes
+    // ---- dequant raw[buf] -> k (bf16): warp per row, lane owns 16 bytes; the
+    // warp's rows are unrolled so their load -> convert -> store chains overlap
+#pragma unroll
     for (int r = warp; r < kBN; r += kWarps) {
       const uint8_t* row = &s.raw[buf][r * kRowBytes];
       const uint4 w = reinterpret_cast<const uint4*>(row)[lane];
       const float sc = reinterpret_cast<const float*>(row + kScaleOff)[lane >> 3];
       uint4 o0, o1;
-      dequant4_hw(w.x, sc, o0.x, o0.y);
-      dequant4_hw(w.y, sc, o0.z, o0.w);
-      dequant4_hw(w.z, sc, o1.x, o1.y);
-      dequant4_hw(w.w, sc, o1.z, o1.w);
+      dequant4_hw_x2(w.x, sc, o0.x, o0.y);
+      dequant4_hw_x2(w.y, sc, o0.z, o0.w);
+      dequant4_hw_x2(w.z, sc, o1.x, o1.y);
+      dequant4_hw_x2(w.w, sc, o1.z, o1.w);
       uint4* dst = reinterpret_cast<uint4*>(&s.k[r * kKStride + lane * 16]);
       dst[0] = o0;
       dst[1] = o1;
@@ -173,8 +184,10 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::kMinBlocks)
 #pragma unroll
     for (int u = 0; u < kTPT; ++u) vt[u] = s.valid[buf][kTPT * sp2 + u] != 0;
     __syncthreads();
-    if (c + 2 < nchunks) issue_gather(s, buf, a, idx_row, req, beg + (c + 2) * kBN, end);
+    if (c + 2 < nchunks) issue_gather(s, buf, a, slot_n);
     cp_async_commit();
+    slot_n = live_slot(a, req, raw_n);
+    raw_n = raw_at(c + 4);
 
     // ---- partial S = Q K^T: tokens 16(w % groups)..+15, d share w / groups
     {

@@ -53,8 +53,8 @@ __global__ void dequant_e4m3_kernel(const uint8_t* __restrict__ in, int64_t n,
 // The decode kernels' in-register dequant, run on its own: rows gathered by
 // slot (int64 byte offsets; slot -1 or >= num_slots gives a zero row), latent
 // bf16(e4m3 * tile scale) through the same device function the decode uses
-// (method 0: dequant4_hw, the general kernel's; method 1: dequant4_hw_x2, the
-// tcgen05 kernel's), rope copied raw.  Reference: the IS_FP8 gather and
+// (method 1: dequant4_hw_x2, the packed-multiply form both decode kernels use;
+// method 0: dequant4_hw, the same arithmetic unpacked), rope copied raw.  Reference: the IS_FP8 gather and
 // dequant of vllm_fp8kv/fp8_ds_mla_sparse_decode.py:136-168 (exact fp32 decode,
 // times the fp32 tile scale, rounded to the query dtype bf16).
 // One thread per 16-byte chunk: chunks 0..31 of a row are latent (16 values,

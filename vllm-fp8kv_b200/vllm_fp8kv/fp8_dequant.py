@@ -72,9 +72,9 @@ def dequant_ds_mla_rows(kv_cache: torch.Tensor, slots: torch.Tensor, method: int
 
     ``kv_cache`` is any uint8 / float8 view of the [num_slots, 656] fp8_ds_mla
     pool (paged shapes are flattened); ``slots`` int32 [n], entries < 0 or
-    >= num_slots give zero rows.  method 0 runs the general decode kernel's
-    dequant, 1 the tcgen05 kernel's; both must equal torch's
-    ``float8_e4m3fn -> float32 * scale -> bfloat16``.
+    >= num_slots give zero rows.  method 1 runs the packed-multiply dequant
+    both decode kernels use, 0 the same arithmetic unpacked; both must equal
+    torch's ``float8_e4m3fn -> float32 * scale -> bfloat16``.
     """
     assert method in (0, 1)
     assert slots.dtype == torch.int32 and slots.dim() == 1
