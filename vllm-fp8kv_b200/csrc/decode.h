@@ -54,10 +54,36 @@ __device__ __forceinline__ int32_t live_slot(const DecodeArgs& a, int32_t req, i
   }
   return (v >= 0 && (int64_t)v < a.num_slots) ? v : -1;
 }
+// Programmatic dependent launch: the decode kernels are launched so that their
+// CTAs may start (and do their setup) while the previous kernel of the stream
+// finishes.  pdl_wait() blocks until that kernel has completed and its writes
+// are visible; no global memory is read or written before it.
+// pdl_launch_dependents() lets the next kernel's CTAs be scheduled early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
 __device__ __forceinline__ int32_t request_of(const DecodeArgs& a, int64_t t) {
   return a.block_table != nullptr ? a.req_id[t] : 0;
 }
 #endif
+
+// Launch `kern` on `st` with programmatic stream serialization (see pdl_wait).
+template <typename Kern>
+cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       const DecodeArgs& a) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
 
 int launch_decode_mma(const DecodeArgs& a, cudaStream_t st);
 int launch_merge_splits(const DecodeArgs& a, cudaStream_t st);

@@ -102,9 +102,11 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::kMinBlocks)
   const int beg = split * a.split_len;
   const int end = min(a.topk, beg + a.split_len);
   const int32_t* idx_row = a.idx + t * a.idx_st + grp * a.idx_sg;
-  const int32_t req = request_of(a, t);
 
   const int nchunks = end > beg ? (end - beg + kBN - 1) / kBN : 0;
+  if (tid == 0) pdl_launch_dependents();
+  pdl_wait();  // the previous kernel of the stream has completed
+  const int32_t req = request_of(a, t);
   // Index prefetch: a chunk's raw top-k entry is loaded two chunks before its
   // gather and turned into a slot (block-table lookup included) one chunk
   // before, so issuing a gather never waits for an index load.
@@ -336,6 +338,8 @@ __global__ void __launch_bounds__(128) merge_splits_kernel(const DecodeArgs a) {
   const int64_t th = blockIdx.x;  // t * H + h
   const int64_t t = th / a.H, h = th % a.H;
   const int S = a.num_splits;
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  pdl_wait();  // the decode kernel's partials are complete
   const float* lse_s = a.ws_lse + th * S;
   float m = -INFINITY;
   for (int i = 0; i < S; ++i) m = fmaxf(m, lse_s[i]);
@@ -382,8 +386,7 @@ int launch_decode_mma(const DecodeArgs& a, cudaStream_t st) {
   auto go = [&](auto kern, size_t smem) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return check_cuda(e, "decode_mma smem attribute");
-    kern<<<grid, kThreads, smem, st>>>(a);
-    return check_cuda(cudaGetLastError(), "decode_mma_kernel launch");
+    return check_cuda(launch_pdl(kern, grid, dim3(kThreads), smem, st, a), "decode_mma_kernel launch");
   };
   const size_t s32 = sizeof(Smem<32>), s64 = sizeof(Smem<64>);
   if (a.q_dtype == FP8MLA_DTYPE_BF16)
@@ -398,11 +401,11 @@ int launch_decode_mma(const DecodeArgs& a, cudaStream_t st) {
 
 int launch_merge_splits(const DecodeArgs& a, cudaStream_t st) {
   dim3 mgrid((unsigned)(a.T * a.H));
-  if (a.q_dtype == FP8MLA_DTYPE_BF16)
-    merge_splits_kernel<__nv_bfloat16><<<mgrid, 128, 0, st>>>(a);
-  else
-    merge_splits_kernel<float><<<mgrid, 128, 0, st>>>(a);
-  return check_cuda(cudaGetLastError(), "merge_splits_kernel launch");
+  const cudaError_t e =
+      a.q_dtype == FP8MLA_DTYPE_BF16
+          ? launch_pdl(merge_splits_kernel<__nv_bfloat16>, mgrid, dim3(128), 0, st, a)
+          : launch_pdl(merge_splits_kernel<float>, mgrid, dim3(128), 0, st, a);
+  return check_cuda(e, "merge_splits_kernel launch");
 }
 
 }  // namespace fp8mla

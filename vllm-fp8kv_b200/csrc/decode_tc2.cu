@@ -358,7 +358,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   c.end = min(a.topk, c.beg + a.split_len);
   c.ntiles = c.end > c.beg ? (c.end - c.beg + kN - 1) / kN : 0;
   c.idx_row = a.idx + t * a.idx_st + grp * a.idx_sg;
-  c.req = request_of(a, t);
+  c.req = 0;  // read after pdl_wait below
   c.sq = smem_u32(s.q);
   c.sk0 = smem_u32(s.k[0]);
   c.sv0 = smem_u32(s.v[0]);
@@ -400,6 +400,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_before();
   cluster_sync_all();  // barriers of both CTAs initialised, tensor memory allocated
   tc_fence_after();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  pdl_wait();  // the previous kernel of the stream has completed: global memory from here on
+  c.req = request_of(a, t);
   c.tmem = s.tmem_base;
   const uint32_t tmem = c.tmem;
 
@@ -601,8 +604,8 @@ int launch_decode_tc2(const DecodeArgs& a, cudaStream_t st) {
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "decode_tc2 smem attribute");
   dim3 grid((unsigned)(a.T * a.G * 2), a.num_splits);
-  tc2::decode_tc2_kernel<<<grid, tc2::kThreads, smem, st>>>(a);
-  int rc = check_cuda(cudaGetLastError(), "decode_tc2_kernel launch");
+  int rc = check_cuda(launch_pdl(tc2::decode_tc2_kernel, grid, dim3(tc2::kThreads), smem, st, a),
+                      "decode_tc2_kernel launch");
   if (rc != FP8MLA_OK || a.num_splits == 1) return rc;
   return launch_merge_splits(a, st);
 }
