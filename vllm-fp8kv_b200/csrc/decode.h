@@ -54,6 +54,33 @@ __device__ __forceinline__ int32_t live_slot(const DecodeArgs& a, int32_t req, i
   }
   return (v >= 0 && (int64_t)v < a.num_slots) ? v : -1;
 }
+// live_slot split in two for software-pipelined gathers: slot_fetch issues
+// the block-table read of a raw index (nothing for flat slots) and
+// slot_finish completes the conversion one pipeline step later, so neither
+// waits on a load issued in the same step.  slot_finish(slot_fetch(v)) ==
+// live_slot(v).
+struct SlotPf {
+  int32_t v;
+  int32_t base;
+};
+__device__ __forceinline__ SlotPf slot_fetch(const DecodeArgs& a, int32_t req, int32_t v) {
+  SlotPf r{v, 0};
+  if (a.block_table != nullptr && v >= 0) {
+    const int32_t blk = v / a.block_size;
+    if (blk < a.max_blocks) r.base = a.block_table[(int64_t)req * a.bt_stride + blk];
+  }
+  return r;
+}
+__device__ __forceinline__ int32_t slot_finish(const DecodeArgs& a, SlotPf p) {
+  int32_t v = p.v;
+  if (a.block_table != nullptr) {
+    if (v < 0) return -1;
+    const int32_t blk = v / a.block_size, off = v - blk * a.block_size;
+    if (blk >= a.max_blocks) return -1;
+    v = (int32_t)((uint32_t)p.base * (uint32_t)a.block_size + (uint32_t)off);
+  }
+  return (v >= 0 && (int64_t)v < a.num_slots) ? v : -1;
+}
 // Programmatic dependent launch: the decode kernels are launched so that their
 // CTAs may start (and do their setup) while the previous kernel of the stream
 // finishes.  pdl_wait() blocks until that kernel has completed and its writes

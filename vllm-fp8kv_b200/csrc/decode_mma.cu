@@ -108,8 +108,9 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::kMinBlocks)
   pdl_wait();  // the previous kernel of the stream has completed
   const int32_t req = request_of(a, t);
   // Index prefetch: a chunk's raw top-k entry is loaded two chunks before its
-  // gather and turned into a slot (block-table lookup included) one chunk
-  // before, so issuing a gather never waits for an index load.
+  // gather, its block-table entry (if any) read one chunk before, and the
+  // slot completed at the gather, so issuing a gather never waits for an
+  // index load.
   const int grow = tid / C::kRowThreads;  // this thread's gather row
   auto raw_at = [&](int ch) -> int32_t {
     const int pos = beg + ch * kBN + grow;
@@ -119,7 +120,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::kMinBlocks)
   cp_async_commit();
   if (nchunks > 1) issue_gather(s, 1, a, live_slot(a, req, raw_at(1)));
   cp_async_commit();
-  int32_t slot_n = live_slot(a, req, raw_at(2));  // chunk c + 2
+  SlotPf slot_n = slot_fetch(a, req, raw_at(2));  // chunk c + 2
   int32_t raw_n = raw_at(3);                      // chunk c + 3
 
   // ---- Q -> smem (bf16), zero rows for padded heads
@@ -186,9 +187,9 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::kMinBlocks)
 #pragma unroll
     for (int u = 0; u < kTPT; ++u) vt[u] = s.valid[buf][kTPT * sp2 + u] != 0;
     __syncthreads();
-    if (c + 2 < nchunks) issue_gather(s, buf, a, slot_n);
+    if (c + 2 < nchunks) issue_gather(s, buf, a, slot_finish(a, slot_n));
     cp_async_commit();
-    slot_n = live_slot(a, req, raw_n);
+    slot_n = slot_fetch(a, req, raw_n);
     raw_n = raw_at(c + 4);
 
     // ---- partial S = Q K^T: tokens 16(w % groups)..+15, d share w / groups
