@@ -270,16 +270,19 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
     return __uint_as_float(tile == 0 ? sc.x : tile == 1 ? sc.y : tile == 2 ? sc.z : sc.w);
   };
   bool ok = true;
-  int32_t nA = c.ntiles > 1 ? slot_at(1, rowA) : -1;
-  int32_t nB = c.ntiles > 1 ? slot_at(1, kOwn * cr + rowB) : -1;
+  // at step j >= 1: slots of tile j+1 (read one step ahead); tiles 0 and 1
+  // are loaded before step 0, with the first three tiles' indices read at once
+  int32_t nA = -1, nB = -1;
   auto step = [&](int j, const Rows& cur, bool vownB, Rows& nxt, bool& vnxt) {
     if (!ok || j >= c.ntiles) return;
-    const int32_t sa1 = nA, sb1 = nB;
-    if (j + 2 < c.ntiles) {
-      nA = slot_at(j + 2, rowA);
-      nB = slot_at(j + 2, kOwn * cr + rowB);
+    if (j >= 1) {
+      const int32_t sa1 = nA, sb1 = nB;
+      if (j + 2 < c.ntiles) {
+        nA = slot_at(j + 2, rowA);
+        nB = slot_at(j + 2, kOwn * cr + rowB);
+      }
+      if (j + 1 < c.ntiles) load(sa1, sb1, nxt, vnxt);
     }
-    if (j + 1 < c.ntiles) load(sa1, sb1, nxt, vnxt);
     const int ks = j % kKStages, vs = j % kVStages;
     if (j >= kKStages) ok = warp_wait_cluster(c.b_kempty + 8 * ks, ((j / kKStages) + 1) & 1, 10);
     if (ok && j >= kVStages)
@@ -325,7 +328,14 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
   };
   Rows A, B;
   bool vA = false, vB = false;
-  if (c.ntiles > 0) load(slot_at(0, rowA), slot_at(0, kOwn * cr + rowB), A, vA);
+  {
+    const int32_t s0A = slot_at(0, rowA), s0B = slot_at(0, kOwn * cr + rowB);
+    const int32_t s1A = slot_at(1, rowA), s1B = slot_at(1, kOwn * cr + rowB);
+    nA = slot_at(2, rowA);
+    nB = slot_at(2, kOwn * cr + rowB);
+    if (c.ntiles > 0) load(s0A, s0B, A, vA);
+    if (c.ntiles > 1) load(s1A, s1B, B, vB);
+  }
   for (int j = 0; j < c.ntiles && ok; j += 2) {
     step(j, A, vA, B, vB);
     step(j + 1, B, vB, A, vA);
@@ -419,25 +429,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint4* qsrc = reinterpret_cast<const uint4*>(
           static_cast<const uint16_t*>(a.q) + t * a.q_st + (int64_t)(hv ? head0 + m : 0) * a.q_sh);
       const uint4 z4 = make_uint4(0, 0, 0, 0);
+      // three load rounds (was seven): dims [384,576) (this thread's 12
+      // chunks) to smem, then dims [0,384) (48 chunks) to tensor memory in
+      // two halves
+      {
+        uint4 x[12];
 #pragma unroll
-      for (int c0 = 0; c0 < kQTmemSteps * 8; c0 += 32) {
-        uint32_t w[32];
+        for (int blk = 0; blk < kQSmemBlocks - 1; ++blk)
 #pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          const uint4 x = hv ? qsrc[c0 / 4 + v] : z4;
-          w[4 * v] = x.x;
-          w[4 * v + 1] = x.y;
-          w[4 * v + 2] = x.z;
-          w[4 * v + 3] = x.w;
-        }
-        tmem_st32(trow + kColQ + c0, w);
+          for (int i = 0; i < 4; ++i) x[4 * blk + i] = hv ? qsrc[kQTmemSteps * 2 + blk * 8 + 4 * hh + i] : z4;
+#pragma unroll
+        for (int blk = 0; blk < kQSmemBlocks - 1; ++blk)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<uint4*>(s.q + blk * kQBlockBytes + swz(m, 4 * hh + i)) = x[4 * blk + i];
       }
 #pragma unroll
-      for (int blk = 0; blk < kQSmemBlocks - 1; ++blk)
+      for (int half = 0; half < 2; ++half) {
+        constexpr int kChunks = kQTmemSteps;  // 16-B chunks per half: 96 columns
+        uint4 x[kChunks];
 #pragma unroll
-        for (int cc = 4 * hh; cc < 4 * hh + 4; ++cc)
-          *reinterpret_cast<uint4*>(s.q + blk * kQBlockBytes + swz(m, cc)) =
-              hv ? qsrc[kQTmemSteps * 2 + blk * 8 + cc] : z4;
+        for (int v = 0; v < kChunks; ++v) x[v] = hv ? qsrc[half * kChunks + v] : z4;
+#pragma unroll
+        for (int c0 = 0; c0 < kChunks * 4; c0 += 32) {
+          uint32_t w[32];
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            w[4 * v] = x[c0 / 4 + v].x;
+            w[4 * v + 1] = x[c0 / 4 + v].y;
+            w[4 * v + 2] = x[c0 / 4 + v].z;
+            w[4 * v + 3] = x[c0 / 4 + v].w;
+          }
+          tmem_st32(trow + kColQ + half * kChunks * 4 + c0, w);
+        }
+      }
       if (hh == 0) {  // mask k-step of Q: bf16 1.0 in column 576, zeros in 577..591
         *reinterpret_cast<uint4*>(s.q + 3 * kQBlockBytes + swz(m, 0)) = make_uint4(0x3F80u, 0, 0, 0);
         *reinterpret_cast<uint4*>(s.q + 3 * kQBlockBytes + swz(m, 1)) = make_uint4(0, 0, 0, 0);
@@ -525,44 +550,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const float inv = lt > 0.f ? 1.f / lt : 0.f;
     const float lse_v = lt > 0.f ? m_used * kLn2 + logf(lt) : -INFINITY;
     const int hh_glob = head0 + m;
+    // O column c of MMA hf holds dim 256 hf + 128 hh + (c mod 128)
+    auto store32 = [&](const uint32_t (&o)[32], int c0) {
+      const int d = 256 * (c0 >> 7) + 128 * hh + (c0 & 127);
+      uint4* dst = a.num_splits == 1
+                       ? reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + t * a.out_st +
+                                                  (int64_t)hh_glob * a.out_sh + d)
+                       // bf16 partials (the output is bf16), merged in fp32 by merge_splits_kernel
+                       : reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.ws_o) +
+                                                  ((t * a.H + hh_glob) * a.num_splits + split) * kNope + d);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        uint32_t w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          w[u] = pack_bf16x2(__uint_as_float(o[8 * v + 2 * u]) * inv,
+                             __uint_as_float(o[8 * v + 2 * u + 1]) * inv);
+        dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    };
+    // two 32-column tensor-memory loads in flight per wait
 #pragma unroll 1
-    for (int c0 = 0; c0 < 256; c0 += 32) {
-      uint32_t o[32];
+    for (int c0 = 0; c0 < 256; c0 += 64) {
+      uint32_t o0[32], o1[32];
       if (have_o) {
-        tmem_ld32(trow + kColO + c0, o);
+        tmem_ld32(trow + kColO + c0, o0);
+        tmem_ld32(trow + kColO + c0 + 32, o1);
         tmem_wait_ld();
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0u;
+        for (int i = 0; i < 32; ++i) o0[i] = o1[i] = 0u;
       }
-      // column c of MMA hf: dim 256 hf + 128 hh + (c mod 128)
-      const int d = 256 * (c0 >> 7) + 128 * hh + (c0 & 127);
-      if (m >= nh) continue;  // padding row (the TMEM load above is warp-collective)
-      if (a.num_splits == 1) {
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + t * a.out_st +
-                                              (int64_t)hh_glob * a.out_sh + d);
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          uint32_t w[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            w[u] = pack_bf16x2(__uint_as_float(o[8 * v + 2 * u]) * inv,
-                               __uint_as_float(o[8 * v + 2 * u + 1]) * inv);
-          dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      } else {
-        // bf16 partials (the output is bf16), merged in fp32 by merge_splits_kernel
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.ws_o) +
-                                              ((t * a.H + hh_glob) * a.num_splits + split) * kNope + d);
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          uint32_t w[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            w[u] = pack_bf16x2(__uint_as_float(o[8 * v + 2 * u]) * inv,
-                               __uint_as_float(o[8 * v + 2 * u + 1]) * inv);
-          dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
-        }
+      if (m < nh) {  // padding rows store nothing (the loads above are warp-collective)
+        store32(o0, c0);
+        store32(o1, c0 + 32);
       }
     }
     if (hh == 0 && m < nh) {
