@@ -86,9 +86,11 @@ FP8MLA_API int64_t fp8mla_decode_workspace_bytes(int64_t T, int64_t H, int64_t G
 
 /*
  * Name of the decode kernel fp8mla_sparse_decode dispatches for this shape
- * ("decode_tc2_kernel" for 128 or 64 heads per kv group with bf16 q, else
- * "decode_mma_kernel"; "+merge_splits_kernel" is appended when the call splits
- * the top-k axis).  Host-only; introspection for benchmarks and profiling.
+ * ("decode_tc2_kernel" for 128 or 64 heads per kv group with bf16 q,
+ * "decode_ws_kernel" for other head counts with bf16 q and a non-empty pool,
+ * "decode_mma_kernel" for fp32 q; "+merge_splits_kernel" is appended when the
+ * call splits the top-k axis; the name string stays valid until the calling
+ * thread's next call).  Host-only; introspection for benchmarks and profiling.
  * No reference counterpart (the reference has one Triton kernel per path).
  */
 FP8MLA_API const char* fp8mla_decode_kernel_name(int64_t T, int64_t H, int64_t G,

@@ -321,7 +321,7 @@ def test_no_on_chip_wait_timed_out(cuda_device):
     assert N.device_status(reset=True) == 0
 
 
-def test_h128_bf16_dispatches_to_tcgen05(cuda_device):
+def test_dispatch_by_heads_and_dtype(cuda_device):
     from vllm_fp8kv.fp8_ds_mla_sparse_decode import decode_kernel_name
 
     assert decode_kernel_name(64, 128, 1, 2048) == "decode_tc2_kernel"
@@ -331,8 +331,11 @@ def test_h128_bf16_dispatches_to_tcgen05(cuda_device):
     # automatic split count doubles to 2
     assert decode_kernel_name(32, 64, 1, 2048) == "decode_tc2_kernel+merge_splits_kernel"
     assert decode_kernel_name(64, 128, 1, 2048, torch.float32) == "decode_mma_kernel"
+    # small head counts with bf16 q: the persistent TMA-gather kernel
     assert decode_kernel_name(256, 16, 1, 2048, torch.bfloat16, 8) == \
-        "decode_mma_kernel+merge_splits_kernel"
+        "decode_ws_kernel+merge_splits_kernel"
+    assert decode_kernel_name(4, 8, 2, 256, torch.bfloat16, 1) == "decode_ws_kernel"
+    assert decode_kernel_name(4, 16, 1, 256, torch.float32, 1) == "decode_mma_kernel"
 
 
 # ------------------------------------------------------------ fused block-table conversion

@@ -120,7 +120,12 @@ int fp8mla_device_status(unsigned int* status, int reset, void* stream) {
   if (status == nullptr) return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "status is NULL");
   *status = 0;
   if (int rc = require_sm100()) return rc;
-  return read_device_status(status, reset != 0, static_cast<cudaStream_t>(stream));
+  // each kernel file keeps its own status word
+  unsigned int v1 = 0, v2 = 0;
+  int rc = read_device_status(&v1, reset != 0, static_cast<cudaStream_t>(stream));
+  if (rc == FP8MLA_OK) rc = read_device_status_ws(&v2, reset != 0, static_cast<cudaStream_t>(stream));
+  *status = v1 | v2;
+  return rc;
 }
 
 int fp8mla_choose_num_splits(int64_t T, int64_t H, int64_t G, int64_t topk, int sm_count) {
@@ -154,10 +159,16 @@ const char* fp8mla_decode_kernel_name(int64_t T, int64_t H, int64_t G, int64_t t
   a.G = (int)G;
   a.topk = (int)topk;
   a.hpg = (int)(H / G);
+  a.block_h = a.hpg < 16 ? a.hpg : 16;
+  a.num_slots = 1;  // names the kernel of a non-empty pool
   a.num_splits = S < 1 ? 1 : S;
-  const bool tc = decode_tc_supported(a);
-  if (a.num_splits > 1) return tc ? "decode_tc2_kernel+merge_splits_kernel" : "decode_mma_kernel+merge_splits_kernel";
-  return tc ? "decode_tc2_kernel" : "decode_mma_kernel";
+  const char* k = decode_tc_supported(a)   ? "decode_tc2_kernel"
+                  : decode_ws_supported(a) ? "decode_ws_kernel"
+                                           : "decode_mma_kernel";
+  if (a.num_splits == 1) return k;
+  static thread_local char buf[64];
+  snprintf(buf, sizeof(buf), "%s+merge_splits_kernel", k);
+  return buf;
 }
 
 }  // extern "C"
@@ -253,6 +264,7 @@ int decode_impl(const void* q, int q_dtype, int64_t T, int64_t H, int64_t q_stri
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (decode_tc_supported(a)) return launch_decode_tc2(a, st);
+  if (decode_ws_supported(a)) return launch_decode_ws(a, device_sm_count(), st);
   return launch_decode_mma(a, st);
 }
 

@@ -96,9 +96,9 @@ __device__ __forceinline__ int32_t request_of(const DecodeArgs& a, int64_t t) {
 #endif
 
 // Launch `kern` on `st` with programmatic stream serialization (see pdl_wait).
-template <typename Kern>
+template <typename Kern, typename... Args>
 cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                       const DecodeArgs& a) {
+                       const Args&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -109,7 +109,7 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, a);
+  return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
 int launch_decode_mma(const DecodeArgs& a, cudaStream_t st);
@@ -117,6 +117,9 @@ int launch_merge_splits(const DecodeArgs& a, cudaStream_t st);
 int read_device_status(unsigned int* status, bool reset, cudaStream_t st);
 bool decode_tc_supported(const DecodeArgs& a);
 int launch_decode_tc2(const DecodeArgs& a, cudaStream_t st);
+bool decode_ws_supported(const DecodeArgs& a);
+int launch_decode_ws(const DecodeArgs& a, int sms, cudaStream_t st);
+int read_device_status_ws(unsigned int* status, bool reset, cudaStream_t st);
 
 int launch_dequant(const uint8_t* in, int64_t n, void* out, int out_dtype, int method,
                    cudaStream_t st);

@@ -74,8 +74,9 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
 }
 
 // Error word written when a bounded wait gives up (host: fp8mla_device_status).
-// Defined here: only decode_tc2.cu includes this header (no relocatable device code).
-__device__ unsigned int g_device_status = 0;
+// Without relocatable device code every translation unit that includes this
+// header has its own copy (internal linkage); each provides a reader.
+static __device__ unsigned int g_device_status = 0;
 constexpr unsigned int kStatusWaitTimeout = 1u;
 // try_wait suspends for a hardware-chosen interval per call; 2^22 calls is
 // well beyond the longest legitimate wait of a CTA (its whole MMA chain, tens
