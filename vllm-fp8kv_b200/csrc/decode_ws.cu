@@ -240,18 +240,22 @@ __device__ void dequant(const DecodeArgs& a, Smem& s, int nunits, int dw, int la
         if (r >= kBN) break;
         const uint8_t* row = rs + (r >> 2) * kGroupBytes + (r & 3) * kRowBytes;
         const bool v = s.valid[st][r] != 0;
-        const uint4 w = reinterpret_cast<const uint4*>(row)[lane];
-        const float sc = reinterpret_cast<const float*>(row + kScaleOff)[lane >> 3];
+        // lane l converts bytes [8l, 8l+8) and [256+8l, 256+8l+8): each of the
+        // two 16-byte stores below is contiguous across the warp
+        const uint2 w0 = reinterpret_cast<const uint2*>(row)[lane];
+        const uint2 w1 = reinterpret_cast<const uint2*>(row + 256)[lane];
+        const float* scl = reinterpret_cast<const float*>(row + kScaleOff);
+        const float sc0 = scl[lane >> 4], sc1 = scl[2 + (lane >> 4)];
         uint4 o0 = make_uint4(0, 0, 0, 0), o1 = make_uint4(0, 0, 0, 0);
         if (v) {
-          dequant4_hw_x2(w.x, sc, o0.x, o0.y);
-          dequant4_hw_x2(w.y, sc, o0.z, o0.w);
-          dequant4_hw_x2(w.z, sc, o1.x, o1.y);
-          dequant4_hw_x2(w.w, sc, o1.z, o1.w);
+          dequant4_hw_x2(w0.x, sc0, o0.x, o0.y);
+          dequant4_hw_x2(w0.y, sc0, o0.z, o0.w);
+          dequant4_hw_x2(w1.x, sc1, o1.x, o1.y);
+          dequant4_hw_x2(w1.y, sc1, o1.z, o1.w);
         }
-        uint4* dst = reinterpret_cast<uint4*>(kst + r * kRowStrideB + lane * 32);
-        dst[0] = o0;
-        dst[1] = o1;
+        uint4* dst = reinterpret_cast<uint4*>(kst + r * kRowStrideB);
+        dst[lane] = o0;
+        dst[32 + lane] = o1;
         if (lane < 8)
           reinterpret_cast<uint4*>(kst + r * kRowStrideB + kNope * 2)[lane] =
               v ? reinterpret_cast<const uint4*>(row + kRopeOff)[lane] : make_uint4(0, 0, 0, 0);
