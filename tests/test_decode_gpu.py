@@ -223,6 +223,24 @@ def test_ragged_topk(cuda_device, topk):
         U.assert_lse_close(lse, ref_lse)
 
 
+def test_many_units_per_cta_with_padded_head_blocks_and_empty_splits(cuda_device):
+    """The small-head kernel is persistent: with 800 units (100 tokens x head
+    blocks of 16 and 8 heads x 4 splits, the last split empty) each CTA walks
+    several units, so rows, Q and state cross unit boundaries."""
+    from vllm_fp8kv import _native as N
+
+    s = synthetic.Shape("u", B=100, H=24, topk=3, ctx=128, pool_slots=100 * 128, mask_frac=0.2)
+    w = synthetic.make_host(s, seed=11)
+    pool = U.device_pool(w.kv_src_bits, check_against_oracle=False)
+    q = U.bf16_tensor(w.q_bits)
+    out, lse = _run(q, pool, torch.from_numpy(w.slots).cuda(), w.sm_scale, num_kv_splits=4)
+    ref, ref_lse = O.sparse_decode(synthetic.bf16_to_f32(w.q_bits),
+                                   pool.view(-1, 656).cpu().numpy(), w.slots, w.sm_scale)
+    U.assert_close(out, ref)
+    U.assert_lse_close(lse, ref_lse)
+    assert N.device_status(reset=True) == 0
+
+
 def test_topk_zero_gives_zeros(cuda_device):
     q = torch.randn(2, 16, 576, device="cuda").bfloat16()
     pool = torch.zeros(64, 656, dtype=torch.uint8, device="cuda")
