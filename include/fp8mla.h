@@ -67,6 +67,24 @@ FP8MLA_API int fp8mla_abi_version(void);
 FP8MLA_API int fp8mla_device_status(unsigned int* status, int reset, void* stream);
 
 /*
+ * Number of mbarrier try_wait calls after which a decode kernel's on-chip
+ * wait gives up (and sets the device status word).  No reference counterpart.
+ */
+FP8MLA_API uint32_t fp8mla_wait_limit(void);
+
+/*
+ * Exercises the error path of the decode kernels' bounded on-chip waits: a
+ * one-warp kernel runs their wait loop on an mbarrier that nothing arrives
+ * on, gives up after `iters` (1 .. fp8mla_wait_limit()) try_wait calls and
+ * returns, leaving bit 0 and "which wait" = 63 in the device status word
+ * (fp8mla_device_status).  *elapsed_ns (if not NULL) receives the loop's
+ * duration, so a caller can see how long a full-limit timeout takes.  No GPU
+ * fault is involved and the context stays usable.  Synchronises `stream`.
+ * For tests and health checks; no reference counterpart.
+ */
+FP8MLA_API int fp8mla_selftest_wait_timeout(uint32_t iters, uint64_t* elapsed_ns, void* stream);
+
+/*
  * Split-KV count the decode picks when called with num_splits = 0.
  * Replaces the host heuristic `_choose_num_kv_splits`
  * (tests/fixtures/triton_mla_sparse_kernel_pr47629.py:406-423): a power of two

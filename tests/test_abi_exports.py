@@ -18,7 +18,7 @@ HEADER = os.path.join(REPO, "include", "fp8mla.h")
 
 def declared_symbols():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:FP8MLA_API\s+)?(?:const\s+char\s*\*|int64_t|int)\s+(fp8mla_\w+)\s*\(",
+    return sorted(set(re.findall(r"^\s*(?:FP8MLA_API\s+)?(?:const\s+char\s*\*|int64_t|uint32_t|int)\s+(fp8mla_\w+)\s*\(",
                                  text, flags=re.M)))
 
 

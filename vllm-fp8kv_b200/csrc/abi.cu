@@ -9,6 +9,7 @@
 
 #include "common.cuh"
 #include "decode.h"
+#include "wait_limit.h"
 
 namespace fp8mla {
 
@@ -127,6 +128,16 @@ int fp8mla_device_status(unsigned int* status, int reset, void* stream) {
   *status = v1 | v2;
   return rc;
 }
+
+int fp8mla_selftest_wait_timeout(uint32_t iters, uint64_t* elapsed_ns, void* stream) {
+  g_last_error[0] = 0;
+  if (iters == 0 || iters > fp8mla_wait_limit())
+    return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "iters must be in [1, %u]", fp8mla_wait_limit());
+  if (int rc = require_sm100()) return rc;
+  return launch_wait_timeout_selftest(iters, elapsed_ns, static_cast<cudaStream_t>(stream));
+}
+
+uint32_t fp8mla_wait_limit(void) { return kMaxWaitIters; }
 
 int fp8mla_choose_num_splits(int64_t T, int64_t H, int64_t G, int64_t topk, int sm_count) {
   if (G <= 0 || H <= 0 || H % G != 0) return 1;

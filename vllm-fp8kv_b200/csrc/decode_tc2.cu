@@ -631,6 +631,38 @@ int launch_decode_tc2(const DecodeArgs& a, cudaStream_t st) {
   return launch_merge_splits(a, st);
 }
 
+namespace {
+// Self-test of the bounded-wait error path: one warp runs the decode kernels'
+// wait loop (warp_wait_n) on an mbarrier that nothing arrives on.  It gives
+// up after `iters` try_wait calls, records the timeout (bits 8.. =
+// kSelftestWhere) and the kernel returns: no fault, the context stays usable.
+constexpr unsigned int kSelftestWhere = 63;
+__device__ unsigned long long g_selftest_ns = 0;
+__global__ void __launch_bounds__(32) wait_timeout_selftest_kernel(uint32_t iters) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(smem_u32(&bar), 1);
+    tc::mbar_init_fence();
+  }
+  __syncwarp();
+  unsigned long long t0, t1;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  (void)tc::warp_wait_n(smem_u32(&bar), 0, kSelftestWhere, iters);
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+  if (threadIdx.x == 0) g_selftest_ns = t1 - t0;
+}
+}  // namespace
+
+int launch_wait_timeout_selftest(uint32_t iters, uint64_t* elapsed_ns, cudaStream_t st) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, st>>>(iters);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  unsigned long long ns = 0;
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&ns, g_selftest_ns, sizeof(ns));
+  if (elapsed_ns != nullptr) *elapsed_ns = ns;
+  return check_cuda(e, "wait timeout self-test");
+}
+
 int read_device_status(unsigned int* status, bool reset, cudaStream_t st) {
   unsigned int v = 0;
   cudaError_t e = cudaMemcpyFromSymbolAsync(&v, tc::g_device_status, sizeof(v), 0,

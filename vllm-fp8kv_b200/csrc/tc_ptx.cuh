@@ -6,6 +6,8 @@
 #pragma once
 #include <stdint.h>
 
+#include "wait_limit.h"
+
 namespace fp8mla {
 namespace tc {
 
@@ -78,17 +80,15 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
 // header has its own copy (internal linkage); each provides a reader.
 static __device__ unsigned int g_device_status = 0;
 constexpr unsigned int kStatusWaitTimeout = 1u;
-// try_wait suspends for a hardware-chosen interval per call; 2^22 calls is
-// well beyond the longest legitimate wait of a CTA (its whole MMA chain, tens
-// of microseconds) yet ends a broken protocol within seconds.
-constexpr uint32_t kMaxWaitIters = 1u << 22;
+using fp8mla::kMaxWaitIters;  // wait_limit.h
 
 // Warp-collective bounded wait: every lane of the calling warp returns the
 // same verdict, so warp-synchronous tcgen05 instructions stay convergent.
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, uint32_t where) {
+__device__ __forceinline__ bool warp_wait_n(uint32_t bar, uint32_t parity, uint32_t where,
+                                            uint32_t iters) {
   uint32_t ok = 0;
   if ((threadIdx.x & 31) == 0) {
-    for (uint32_t it = 0; it < kMaxWaitIters; ++it) {
+    for (uint32_t it = 0; it < iters; ++it) {
       if (mbar_try_wait(bar, parity)) {
         ok = 1;
         break;
@@ -99,6 +99,9 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, uint32_
   ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
   __syncwarp();
   return ok != 0;
+}
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, uint32_t where) {
+  return warp_wait_n(bar, parity, where, kMaxWaitIters);
 }
 
 // Single-thread bounded wait (the MMA issuer).

@@ -27,6 +27,8 @@ SIGNATURES = {
     "fp8mla_last_error": (ctypes.c_char_p, []),
     "fp8mla_abi_version": (_I32, []),
     "fp8mla_device_status": (_I32, [ctypes.POINTER(ctypes.c_uint), _I32, _P]),
+    "fp8mla_selftest_wait_timeout": (_I32, [ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint64), _P]),
+    "fp8mla_wait_limit": (ctypes.c_uint32, []),
     "fp8mla_choose_num_splits": (_I32, [_I64, _I64, _I64, _I64, _I32]),
     "fp8mla_decode_workspace_bytes": (_I64, [_I64, _I64, _I64, _I64, _I32]),
     "fp8mla_decode_kernel_name": (ctypes.c_char_p, [_I64, _I64, _I64, _I64, _I32, _I32]),
