@@ -193,16 +193,6 @@ __device__ __forceinline__ void dequant4_hw_x2(uint32_t w, float s, uint32_t& lo
   hi = pack_bf16x2(f23.x, f23.y);
 }
 
-// Tile scale preparation for dequant4_bf16.
-__device__ __forceinline__ void prep_scale(float s, float& scale_x, bool& fused) {
-  float sx = s * 1.329227995784915872903807060280344576e36f;  // * 2^120
-  fused = fabsf(sx) < 3.0e38f;  // finite and not overflowing (also false for NaN)
-  scale_x = fused ? sx : s;
-}
 
-// Round a float to a bf16-representable float (RNE).
-__device__ __forceinline__ float round_bf16(float x) {
-  return __bfloat162float(__float2bfloat16_rn(x));
-}
 
 }  // namespace fp8mla
