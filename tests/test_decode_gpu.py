@@ -398,6 +398,35 @@ def test_paged_decode_equals_convert_then_decode(cuda_device, H, splits):
     U.assert_lse_close(fused_lse.cpu().numpy(), ref_lse)
 
 
+@pytest.mark.parametrize("H", [128, 16])
+def test_paged_decode_with_non_power_of_two_pages(cuda_device, H):
+    """Pages of 48 slots take the division path of the position -> block step
+    (powers of two take a shift): still bit-identical to convert-then-decode."""
+    from vllm_fp8kv.fp8_ds_mla_sparse_decode import fp8_ds_mla_sparse_decode_paged
+    from vllm_fp8kv.index_convert import convert_req_index_to_global_index
+
+    bs, B, T, topk, max_blocks = 48, 3, 6, 256, 40
+    shape = synthetic.Shape("paged48", B=B, H=H, topk=topk, ctx=1024, pool_slots=8192, mask_frac=0.1)
+    w = synthetic.make_host(shape, seed=3)
+    pool = U.device_pool(w.kv_src_bits, check_against_oracle=False)
+    rng = np.random.default_rng(4)
+    n_blocks = 8192 // bs
+    bt = rng.integers(0, n_blocks, size=(B, max_blocks)).astype(np.int32)
+    req = rng.integers(0, B, size=T).astype(np.int32)
+    tok = np.stack([rng.choice(max_blocks * bs + 96, size=topk, replace=False) for _ in range(T)])
+    tok = tok.astype(np.int32)
+    tok[:, ::29] = -1
+    q = torch.randn((T, H, 576), generator=torch.Generator().manual_seed(H)).bfloat16().cuda()
+    req_t, bt_t, tok_t = (torch.from_numpy(x).cuda() for x in (req, bt, tok))
+    slots = convert_req_index_to_global_index(req_t, bt_t, tok_t, BLOCK_SIZE=bs, NUM_TOPK_TOKENS=topk)
+    assert np.array_equal(slots.cpu().numpy(), O.convert_req_index(req, bt, tok, bs))
+    flat, flat_lse = fp8_ds_mla_sparse_decode(q, pool, slots, w.sm_scale, return_lse=True)
+    fused, fused_lse = fp8_ds_mla_sparse_decode_paged(q, pool, req_t, bt_t, tok_t, w.sm_scale,
+                                                      block_size=bs, return_lse=True)
+    torch.cuda.synchronize()
+    assert torch.equal(fused, flat) and torch.equal(fused_lse, flat_lse)
+
+
 def test_paged_decode_rejects_bad_tables(cuda_device):
     from vllm_fp8kv.fp8_ds_mla_sparse_decode import fp8_ds_mla_sparse_decode_paged
 

@@ -272,6 +272,9 @@ int decode_impl(const void* q, int q_dtype, int64_t T, int64_t H, int64_t q_stri
     a.bt_stride = paged->bt_stride;
     a.max_blocks = paged->max_blocks;
     a.block_size = (int)paged->block_size;
+    a.block_shift = -1;
+    for (int k = 0; k < 31; ++k)
+      if ((int64_t)1 << k == paged->block_size) a.block_shift = k;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (decode_tc_supported(a)) return launch_decode_tc2(a, st);

@@ -36,6 +36,7 @@ struct DecodeArgs {
   int64_t bt_stride;
   int64_t max_blocks;
   int block_size;
+  int block_shift;   // log2(block_size) when it is a power of two, else -1
 };
 
 #ifdef __CUDACC__
@@ -44,10 +45,15 @@ struct DecodeArgs {
 // The block-table step is vLLM's converter with its int32 arithmetic
 // (installed vllm/v1/attention/backends/mla/sparse_utils.py:11-78; the
 // library's standalone form is convert_req_index_kernel).
+// Block of a non-negative position: a shift for power-of-two pages (the
+// usual 64), a division otherwise.
+__device__ __forceinline__ int32_t block_of(const DecodeArgs& a, int32_t v) {
+  return a.block_shift >= 0 ? (v >> a.block_shift) : v / a.block_size;
+}
 __device__ __forceinline__ int32_t live_slot(const DecodeArgs& a, int32_t req, int32_t v) {
   if (a.block_table != nullptr) {
     if (v < 0) return -1;
-    const int32_t blk = v / a.block_size, off = v - blk * a.block_size;
+    const int32_t blk = block_of(a, v), off = v - blk * a.block_size;
     if (blk >= a.max_blocks) return -1;
     const uint32_t base = (uint32_t)a.block_table[(int64_t)req * a.bt_stride + blk];
     v = (int32_t)(base * (uint32_t)a.block_size + (uint32_t)off);
@@ -66,7 +72,7 @@ struct SlotPf {
 __device__ __forceinline__ SlotPf slot_fetch(const DecodeArgs& a, int32_t req, int32_t v) {
   SlotPf r{v, 0};
   if (a.block_table != nullptr && v >= 0) {
-    const int32_t blk = v / a.block_size;
+    const int32_t blk = block_of(a, v);
     if (blk < a.max_blocks) r.base = a.block_table[(int64_t)req * a.bt_stride + blk];
   }
   return r;
@@ -75,7 +81,7 @@ __device__ __forceinline__ int32_t slot_finish(const DecodeArgs& a, SlotPf p) {
   int32_t v = p.v;
   if (a.block_table != nullptr) {
     if (v < 0) return -1;
-    const int32_t blk = v / a.block_size, off = v - blk * a.block_size;
+    const int32_t blk = block_of(a, v), off = v - blk * a.block_size;
     if (blk >= a.max_blocks) return -1;
     v = (int32_t)((uint32_t)p.base * (uint32_t)a.block_size + (uint32_t)off);
   }

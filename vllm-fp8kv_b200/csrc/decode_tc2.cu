@@ -222,6 +222,11 @@ __device__ void mma_role(const Ctx& c) {
 }
 
 // ------------------------------------------------------------------ gather + dequant
+// kPaged: the index entries are request-local positions resolved through the
+// block table; the index pipeline then runs one tile deeper (raw entry three
+// tiles ahead, block-table read two ahead, slot one ahead) so that no step
+// waits on the two dependent loads of a position.
+template <bool kPaged>
 __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
   const DecodeArgs& a = *c.a;
   const int cr = (int)c.rank;
@@ -230,10 +235,11 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
   // part B: own row rowB (tile row kOwn*cr + rowB), lane eighth qB
   const int rowB = lw * 4 + (lane >> 3), qB = lane & 7;
   const bool ownA = (rowA >> 5) == cr;
-  auto slot_at = [&](int jt, int row) -> int32_t {
+  auto raw_at = [&](int jt, int row) -> int32_t {
     const int pos = c.beg + jt * kN + row;
-    return pos < c.end ? live_slot(a, c.req, c.idx_row[pos]) : -1;
+    return pos < c.end ? c.idx_row[pos] : -1;
   };
+  auto slot_at = [&](int jt, int row) -> int32_t { return live_slot(a, c.req, raw_at(jt, row)); };
   // vb: own row rowB is live (its mask column is 0, else -inf)
   auto load = [&](int32_t sa, int32_t sb, Rows& R, bool& vb) {
     vb = sb >= 0;
@@ -273,13 +279,25 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
   // at step j >= 1: slots of tile j+1 (read one step ahead); tiles 0 and 1
   // are loaded before step 0, with the first three tiles' indices read at once
   int32_t nA = -1, nB = -1;
+  SlotPf fA{-1, 0}, fB{-1, 0};  // paged: block-table reads of tile j+1 (at step j >= 1)
   auto step = [&](int j, const Rows& cur, bool vownB, Rows& nxt, bool& vnxt) {
     if (!ok || j >= c.ntiles) return;
     if (j >= 1) {
-      const int32_t sa1 = nA, sb1 = nB;
-      if (j + 2 < c.ntiles) {
-        nA = slot_at(j + 2, rowA);
-        nB = slot_at(j + 2, kOwn * cr + rowB);
+      int32_t sa1, sb1;
+      if constexpr (kPaged) {
+        sa1 = slot_finish(a, fA);
+        sb1 = slot_finish(a, fB);
+        fA = slot_fetch(a, c.req, nA);  // nA / nB: raw entries of tile j+2
+        fB = slot_fetch(a, c.req, nB);
+        nA = raw_at(j + 3, rowA);
+        nB = raw_at(j + 3, kOwn * cr + rowB);
+      } else {
+        sa1 = nA;
+        sb1 = nB;
+        if (j + 2 < c.ntiles) {
+          nA = slot_at(j + 2, rowA);
+          nB = slot_at(j + 2, kOwn * cr + rowB);
+        }
       }
       if (j + 1 < c.ntiles) load(sa1, sb1, nxt, vnxt);
     }
@@ -331,8 +349,15 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
   {
     const int32_t s0A = slot_at(0, rowA), s0B = slot_at(0, kOwn * cr + rowB);
     const int32_t s1A = slot_at(1, rowA), s1B = slot_at(1, kOwn * cr + rowB);
-    nA = slot_at(2, rowA);
-    nB = slot_at(2, kOwn * cr + rowB);
+    if constexpr (kPaged) {
+      fA = slot_fetch(a, c.req, raw_at(2, rowA));
+      fB = slot_fetch(a, c.req, raw_at(2, kOwn * cr + rowB));
+      nA = raw_at(3, rowA);
+      nB = raw_at(3, kOwn * cr + rowB);
+    } else {
+      nA = slot_at(2, rowA);
+      nB = slot_at(2, kOwn * cr + rowB);
+    }
     if (c.ntiles > 0) load(s0A, s0B, A, vA);
     if (c.ntiles > 1) load(s1A, s1B, B, vB);
   }
@@ -344,6 +369,7 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
 
 }  // namespace
 
+template <bool kPaged>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     decode_tc2_kernel(const DecodeArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -599,7 +625,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ================================================= gather + dequant
-    load_role(c, s, warp - kFirstLoadWarp, lane);
+    load_role<kPaged>(c, s, warp - kFirstLoadWarp, lane);
   }
 
   // both CTAs: no MMA of the pair may still run, no arrival may still target
@@ -621,12 +647,15 @@ bool decode_tc_supported(const DecodeArgs& a) {
 
 int launch_decode_tc2(const DecodeArgs& a, cudaStream_t st) {
   const size_t smem = sizeof(tc2::Smem) + 1024;  // + alignment slack
-  cudaError_t e = cudaFuncSetAttribute(tc2::decode_tc2_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return check_cuda(e, "decode_tc2 smem attribute");
-  dim3 grid((unsigned)(a.T * a.G * 2), a.num_splits);
-  int rc = check_cuda(launch_pdl(tc2::decode_tc2_kernel, grid, dim3(tc2::kThreads), smem, st, a),
+  auto go = [&](auto kern) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return check_cuda(e, "decode_tc2 smem attribute");
+    dim3 grid((unsigned)(a.T * a.G * 2), a.num_splits);
+    return check_cuda(launch_pdl(kern, grid, dim3(tc2::kThreads), smem, st, a),
                       "decode_tc2_kernel launch");
+  };
+  const int rc = a.block_table != nullptr ? go(tc2::decode_tc2_kernel<true>)
+                                          : go(tc2::decode_tc2_kernel<false>);
   if (rc != FP8MLA_OK || a.num_splits == 1) return rc;
   return launch_merge_splits(a, st);
 }
