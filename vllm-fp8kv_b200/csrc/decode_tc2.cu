@@ -47,7 +47,9 @@
 //               per row, 8 rows per warp), part B = the other half and the
 //               rope of the 32 own rows (8 lanes per row, 4 rows per warp);
 //               registers hold the next tile's rows while this tile is
-//               written, slots are read two tiles ahead.
+//               written, slots are read two tiles ahead (with a block table,
+//               the kPaged instantiation: raw positions three tiles ahead,
+//               block-table entries two ahead).
 // Barriers that gate the issuing thread (tile data, P, Q) live in the even
 // CTA and count arrivals of both CTAs (one per warp; the odd CTA's by remote
 // arrive); completion of pair MMAs is signalled to both CTAs by a multicast
