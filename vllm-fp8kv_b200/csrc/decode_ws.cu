@@ -234,32 +234,47 @@ __device__ void dequant(const DecodeArgs& a, Smem& s, int nunits, int dw, int la
         ok = warp_wait(smem_u32(&s.k_empty[ks]), ((g / kKStages) + 1) & 1, 23);
       const uint8_t* rs = s.raw[st];
       uint8_t* kst = reinterpret_cast<uint8_t*>(s.k[ks]);
+      // all of this warp's rows are loaded before any is converted, so their
+      // shared-memory loads and conversion chains overlap.  Lane l converts
+      // bytes [8l, 8l+8) and [256+8l, 256+8l+8): each of the two 16-byte
+      // stores per row is contiguous across the warp.
+      uint2 w0[kRowsPerDequantWarp], w1[kRowsPerDequantWarp];
+      float sc0[kRowsPerDequantWarp], sc1[kRowsPerDequantWarp];
+      uint4 rope[kRowsPerDequantWarp];
+      bool vrow[kRowsPerDequantWarp];
 #pragma unroll
       for (int i = 0; i < kRowsPerDequantWarp; ++i) {
         const int r = dw + kDequantWarps * i;
-        if (r >= kBN) break;
-        const uint8_t* row = rs + (r >> 2) * kGroupBytes + (r & 3) * kRowBytes;
-        const bool v = s.valid[st][r] != 0;
-        // lane l converts bytes [8l, 8l+8) and [256+8l, 256+8l+8): each of the
-        // two 16-byte stores below is contiguous across the warp
-        const uint2 w0 = reinterpret_cast<const uint2*>(row)[lane];
-        const uint2 w1 = reinterpret_cast<const uint2*>(row + 256)[lane];
-        const float* scl = reinterpret_cast<const float*>(row + kScaleOff);
-        const float sc0 = scl[lane >> 4], sc1 = scl[2 + (lane >> 4)];
-        uint4 o0 = make_uint4(0, 0, 0, 0), o1 = make_uint4(0, 0, 0, 0);
-        if (v) {
-          dequant4_hw_x2(w0.x, sc0, o0.x, o0.y);
-          dequant4_hw_x2(w0.y, sc0, o0.z, o0.w);
-          dequant4_hw_x2(w1.x, sc1, o1.x, o1.y);
-          dequant4_hw_x2(w1.y, sc1, o1.z, o1.w);
+        if (r < kBN) {
+          const uint8_t* row = rs + (r >> 2) * kGroupBytes + (r & 3) * kRowBytes;
+          vrow[i] = s.valid[st][r] != 0;
+          w0[i] = reinterpret_cast<const uint2*>(row)[lane];
+          w1[i] = reinterpret_cast<const uint2*>(row + 256)[lane];
+          const float* scl = reinterpret_cast<const float*>(row + kScaleOff);
+          sc0[i] = scl[lane >> 4];
+          sc1[i] = scl[2 + (lane >> 4)];
+          rope[i] = lane < 8 ? reinterpret_cast<const uint4*>(row + kRopeOff)[lane] : make_uint4(0, 0, 0, 0);
         }
-        uint4* dst = reinterpret_cast<uint4*>(kst + r * kRowStrideB);
-        dst[lane] = o0;
-        dst[32 + lane] = o1;
-        if (lane < 8)
-          reinterpret_cast<uint4*>(kst + r * kRowStrideB + kNope * 2)[lane] =
-              v ? reinterpret_cast<const uint4*>(row + kRopeOff)[lane] : make_uint4(0, 0, 0, 0);
-        if (lane == 0) s.kvalid[ks][r] = v ? 1 : 0;
+      }
+#pragma unroll
+      for (int i = 0; i < kRowsPerDequantWarp; ++i) {
+        const int r = dw + kDequantWarps * i;
+        if (r < kBN) {
+          uint4 o0 = make_uint4(0, 0, 0, 0), o1 = make_uint4(0, 0, 0, 0);
+          if (vrow[i]) {
+            dequant4_hw_x2(w0[i].x, sc0[i], o0.x, o0.y);
+            dequant4_hw_x2(w0[i].y, sc0[i], o0.z, o0.w);
+            dequant4_hw_x2(w1[i].x, sc1[i], o1.x, o1.y);
+            dequant4_hw_x2(w1[i].y, sc1[i], o1.z, o1.w);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(kst + r * kRowStrideB);
+          dst[lane] = o0;
+          dst[32 + lane] = o1;
+          if (lane < 8)
+            reinterpret_cast<uint4*>(kst + r * kRowStrideB + kNope * 2)[lane] =
+                vrow[i] ? rope[i] : make_uint4(0, 0, 0, 0);
+          if (lane == 0) s.kvalid[ks][r] = vrow[i] ? 1 : 0;
+        }
       }
       __syncwarp();
       if (lane == 0) {
