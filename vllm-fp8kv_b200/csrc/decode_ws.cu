@@ -230,8 +230,6 @@ __device__ void dequant(const DecodeArgs& a, Smem& s, int nunits, int dw, int la
     for (int c = 0; c < nch; ++c, ++g) {
       const int st = g % kRawStages, ks = g % kKStages;
       if (ok) ok = warp_acquire(smem_u32(&s.raw_full[st]), (g / kRawStages) & 1, 22);
-      if (g >= kKStages && ok)
-        ok = warp_wait(smem_u32(&s.k_empty[ks]), ((g / kKStages) + 1) & 1, 23);
       const uint8_t* rs = s.raw[st];
       uint8_t* kst = reinterpret_cast<uint8_t*>(s.k[ks]);
       // all of this warp's rows are loaded before any is converted, so their
@@ -256,6 +254,12 @@ __device__ void dequant(const DecodeArgs& a, Smem& s, int nunits, int dw, int la
           rope[i] = lane < 8 ? reinterpret_cast<const uint4*>(row + kRopeOff)[lane] : make_uint4(0, 0, 0, 0);
         }
       }
+      // the raw stage is consumed (its values are in registers): hand it back
+      // to the producer, then wait for the K stage
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&s.raw_empty[st]));
+      if (g >= kKStages && ok)
+        ok = warp_wait(smem_u32(&s.k_empty[ks]), ((g / kKStages) + 1) & 1, 23);
 #pragma unroll
       for (int i = 0; i < kRowsPerDequantWarp; ++i) {
         const int r = dw + kDequantWarps * i;
@@ -277,10 +281,7 @@ __device__ void dequant(const DecodeArgs& a, Smem& s, int nunits, int dw, int la
         }
       }
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(smem_u32(&s.raw_empty[st]));
-        mbar_arrive(smem_u32(&s.k_full[ks]));
-      }
+      if (lane == 0) mbar_arrive(smem_u32(&s.k_full[ks]));
     }
   }
 }
