@@ -13,7 +13,7 @@
 //               to a slot; lanes 0-7 each issue one TMA tile::gather4 of four
 //               whole 656-byte rows into a stage of the raw ring (masked rows
 //               fetch row 0 and are flagged invalid).  At each unit start it
-//               bulk-copies the unit's Q rows into one of two Q buffers.
+//               bulk-copies the unit's Q rows into the Q buffer.
 //   warps 1-7   dequant.  Raw ring -> bf16 key rows of a two-stage K ring
 //               (e4m3 * tile scale in fp32, RNE to bf16; rope copied raw),
 //               invalid rows written as zeros, validity flags alongside.
@@ -44,13 +44,14 @@ namespace {
 
 constexpr int kBN = 32;                       // tokens per chunk
 constexpr int kBH = 16;                       // heads per unit
-constexpr int kRawStages = 4;
+constexpr int kRawStages = 5;
 constexpr int kGroupBytes = 2688;             // 4 rows (2624 B) padded to a multiple of 128
 constexpr int kRawStageBytes = 8 * kGroupBytes;
 constexpr int kChunkTx = kBN * kRowBytes;     // bytes a chunk's eight gather4 deliver
 constexpr int kKStride = 584;                 // bf16 per K / Q row: 576 + 8 (bank spread)
 constexpr int kRowStrideB = kKStride * 2;     // 1168 B
 constexpr int kKStages = 2;
+constexpr int kQBufs = 1;                     // Q moves to registers at each unit start
 constexpr int kPStride = kBN + 8;             // bf16 per P row
 constexpr int kDequantWarps = 7;  // 16 warps in all: 128 registers a thread
 constexpr int kRowsPerDequantWarp = (kBN + kDequantWarps - 1) / kDequantWarps;  // at most
@@ -67,7 +68,7 @@ constexpr int kThreads = (kFirstCompute + kComputeWarps) * 32;
 
 struct Smem {
   uint8_t raw[kRawStages][kRawStageBytes];    // 128-B aligned gather4 destinations
-  uint16_t q[2][kBH * kKStride];
+  uint16_t q[kQBufs][kBH * kKStride];
   uint16_t k[kKStages][kBN * kKStride];
   uint16_t p[kBH * kPStride];
   float sp[kDParts][kBH][kBN + 1];            // partial S per d share
@@ -78,7 +79,7 @@ struct Smem {
   uint8_t kvalid[kKStages][kBN];
   uint64_t raw_full[kRawStages], raw_empty[kRawStages];
   uint64_t k_full[kKStages], k_empty[kKStages];
-  uint64_t q_full[2], q_empty[2];
+  uint64_t q_full[kQBufs], q_empty[kQBufs];
 };
 static_assert(offsetof(Smem, q) % 16 == 0 && offsetof(Smem, k) % 16 == 0 &&
                   offsetof(Smem, p) % 16 == 0 && offsetof(Smem, raw_full) % 8 == 0,
@@ -184,9 +185,9 @@ __device__ void producer(const DecodeArgs& a, Smem& s, const CUtensorMap* tm, in
     if (x.nch == 0) continue;
     const int32_t req = request_of(a, x.t);
     // the unit's Q rows -> Q buffer qc & 1, once the compute warps are done with it
-    const int qb = qc & 1;
+    const int qb = qc % kQBufs;
     const uint32_t qfull = smem_u32(&s.q_full[qb]);
-    if (qc >= 2 && ok) ok = warp_wait(smem_u32(&s.q_empty[qb]), ((qc >> 1) + 1) & 1, 20);
+    if (qc >= kQBufs && ok) ok = warp_wait(smem_u32(&s.q_empty[qb]), ((qc / kQBufs) + 1) & 1, 20);
     if (lane == 0) mbar_arrive_expect_tx(qfull, (uint32_t)x.nh * kDqk * 2);
     __syncwarp();
     if (lane < x.nh)
@@ -309,8 +310,8 @@ __device__ void compute(const DecodeArgs& a, Smem& s, int nunits, int cw, int la
     for (int i = 0; i < kOutTiles; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;   // head sh (shared by its 16 threads)
     if (x.nch > 0) {
-      const int qb = qc & 1;
-      if (ok) ok = warp_acquire(smem_u32(&s.q_full[qb]), (qc >> 1) & 1, 24);
+      const int qb = qc % kQBufs;
+      if (ok) ok = warp_acquire(smem_u32(&s.q_full[qb]), (qc / kQBufs) & 1, 24);
       uint32_t qf[kPartSteps][4];
       {
         const uint32_t qa0 = smem_u32(s.q[qb]) + (((lane & 15) * kKStride + (lane >> 4) * 8) << 1);
@@ -454,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&s.k_full[i]), kDequantWarps);
       mbar_init(smem_u32(&s.k_empty[i]), kComputeWarps);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kQBufs; ++i) {
       mbar_init(smem_u32(&s.q_full[i]), 1);
       mbar_init(smem_u32(&s.q_empty[i]), kComputeWarps);
     }
@@ -462,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   // Q buffers start zeroed: a unit with fewer than 16 heads leaves its padding
   // rows finite (they are computed and never stored)
-  for (int i = threadIdx.x; i < 2 * kBH * kKStride / 8; i += kThreads)
+  for (int i = threadIdx.x; i < kQBufs * kBH * kKStride / 8; i += kThreads)
     reinterpret_cast<uint4*>(s.q)[i] = make_uint4(0, 0, 0, 0);
   fence_proxy_async_smem();  // the zeros before any bulk copy into the buffers
   __syncthreads();
