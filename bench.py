@@ -157,6 +157,30 @@ def cpu_reference_step_fn(shape_name: str, sample_requests: int, seed: int = 0):
     return fn, B * s.topk * 656, desc
 
 
+def shard_seeds(rank: int) -> tuple[int, int]:
+    """Seeds of rank's shard: its own pool and requests, and its rotating
+    q / top-k sets (weak scaling: every rank holds different data)."""
+    return 1000 + rank, 2000 + rank
+
+
+def max_over_ranks(values, dist, device) -> list[float]:
+    """Element-wise max of per-rank timings, on every rank (the slowest rank
+    sets the job's step time).  `dist` is torch.distributed or None for one
+    process.  Runs after the timed regions, never inside them."""
+    import torch
+
+    v = torch.tensor(list(values), dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    return v.tolist()
+
+
+def job_kv_gbs(world: int, kv_bytes_per_rank: int, ms: float) -> float:
+    """KV GB/s of the whole job: every rank moves its own rows in `ms`."""
+    return world * kv_bytes_per_rank / (ms * 1e-3) / 1e9
+
+
 def run_reference_arm(args, rank):
     if rank != 0:
         return None
@@ -210,10 +234,11 @@ def run_ours(args, rank, world, local_rank):
                                 device_id=dev)
 
     s = synthetic.SHAPES[args.workload]
-    w = synthetic.make_device(s, seed=1000 + rank, device=dev)
+    pool_seed, set_seed = shard_seeds(rank)
+    w = synthetic.make_device(s, seed=pool_seed, device=dev)
     splits = s.num_splits or None
     # rotating input sets over the same pool: fresh top-k rows every step
-    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    g = torch.Generator(device=dev).manual_seed(set_seed)
     sets = [(w.q, w.slots)]
     for _ in range(N_SETS - 1):
         tok = torch.rand((s.B, s.ctx), generator=g, device=dev).argsort(dim=1)[:, : s.topk]
@@ -332,11 +357,7 @@ def run_ours(args, rank, world, local_rank):
     d2h_b = hout[0].numel() * 2 + hlse[0].numel() * 4
 
     # ---- max over ranks (no collective on the hot path; this is after timing)
-    vals = torch.tensor([step_ms, e2e_ms, launch_ms], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-        dist.barrier()
-    step_ms, e2e_ms, launch_ms = vals.tolist()
+    step_ms, e2e_ms, launch_ms = max_over_ranks([step_ms, e2e_ms, launch_ms], dist, dev)
 
     from vllm_fp8kv.fp8_ds_mla_sparse_decode import decode_kernel_name
 
@@ -366,7 +387,7 @@ def run_ours(args, rank, world, local_rank):
         roof["traffic"] = _traffic_per_launch(kern, args.workload)
         roof["algorithmic_bytes_per_launch"] = alg
         roof["algorithmic_flops_per_launch"] = flops
-        value = world * kvb / (step_ms * 1e-3) / 1e9
+        value = job_kv_gbs(world, kvb, step_ms)
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
@@ -383,7 +404,7 @@ def run_ours(args, rank, world, local_rank):
             },
             "tflops": world * flops / (step_ms * 1e-3) / 1e12,
             "roofline": roof,
-            "e2e": {"value": world * kvb / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+            "e2e": {"value": job_kv_gbs(world, kvb, e2e_ms), "unit": "GB/s",
                     "us_per_call": e2e_ms * 1e3, "h2d_bytes_per_step": h2d_b,
                     "d2h_bytes_per_step": d2h_b},
             "gpu_launches": args.steps * launches_per_step,
