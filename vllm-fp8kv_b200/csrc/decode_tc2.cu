@@ -237,11 +237,19 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
   // part B: own row rowB (tile row kOwn*cr + rowB), lane eighth qB
   const int rowB = lw * 4 + (lane >> 3), qB = lane & 7;
   const bool ownA = (rowA >> 5) == cr;
-  auto raw_at = [&](int jt, int row) -> int32_t {
-    const int pos = c.beg + jt * kN + row;
-    return pos < c.end ? c.idx_row[pos] : -1;
+  // A warp's tile rows are 8 part-A rows and 4 own part-B rows: lane i < 8
+  // converts the index of part-A row lw*8 + i, lane 8 + i (i < 4) that of own
+  // row lw*4 + i, and the slots reach the lanes that gather them by shuffle.
+  const int irow = lane < 8 ? lw * 8 + lane : (lane < 12 ? kOwn * cr + lw * 4 + (lane - 8) : -1);
+  auto raw_at = [&](int jt) -> int32_t {
+    const int pos = c.beg + jt * kN + irow;
+    return (irow >= 0 && pos < c.end) ? c.idx_row[pos] : -1;
   };
-  auto slot_at = [&](int jt, int row) -> int32_t { return live_slot(a, c.req, raw_at(jt, row)); };
+  auto slot_at = [&](int jt) -> int32_t { return live_slot(a, c.req, raw_at(jt)); };
+  auto share = [&](int32_t sl, int32_t& sa, int32_t& sb) {
+    sa = __shfl_sync(0xFFFFFFFFu, sl, lane & 7);         // part-A row of this lane
+    sb = __shfl_sync(0xFFFFFFFFu, sl, 8 + (lane >> 3));  // own part-B row of this lane
+  };
   // vb: own row rowB is live (its mask column is 0, else -inf)
   auto load = [&](int32_t sa, int32_t sb, Rows& R, bool& vb) {
     vb = sb >= 0;
@@ -280,27 +288,22 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
   bool ok = true;
   // at step j >= 1: slots of tile j+1 (read one step ahead); tiles 0 and 1
   // are loaded before step 0, with the first three tiles' indices read at once
-  int32_t nA = -1, nB = -1;
-  SlotPf fA{-1, 0}, fB{-1, 0};  // paged: block-table reads of tile j+1 (at step j >= 1)
+  int32_t nI = -1;       // flat: slot of tile j+1; paged: raw entry of tile j+2
+  SlotPf fI{-1, 0};       // paged: block-table read of tile j+1 (at step j >= 1)
   auto step = [&](int j, const Rows& cur, bool vownB, Rows& nxt, bool& vnxt) {
     if (!ok || j >= c.ntiles) return;
     if (j >= 1) {
-      int32_t sa1, sb1;
+      int32_t s1;
       if constexpr (kPaged) {
-        sa1 = slot_finish(a, fA);
-        sb1 = slot_finish(a, fB);
-        fA = slot_fetch(a, c.req, nA);  // nA / nB: raw entries of tile j+2
-        fB = slot_fetch(a, c.req, nB);
-        nA = raw_at(j + 3, rowA);
-        nB = raw_at(j + 3, kOwn * cr + rowB);
+        s1 = slot_finish(a, fI);
+        fI = slot_fetch(a, c.req, nI);
+        nI = raw_at(j + 3);
       } else {
-        sa1 = nA;
-        sb1 = nB;
-        if (j + 2 < c.ntiles) {
-          nA = slot_at(j + 2, rowA);
-          nB = slot_at(j + 2, kOwn * cr + rowB);
-        }
+        s1 = nI;
+        if (j + 2 < c.ntiles) nI = slot_at(j + 2);
       }
+      int32_t sa1, sb1;
+      share(s1, sa1, sb1);
       if (j + 1 < c.ntiles) load(sa1, sb1, nxt, vnxt);
     }
     const int ks = j % kKStages, vs = j % kVStages;
@@ -349,17 +352,16 @@ __device__ void load_role(const Ctx& c, Smem& s, int lw, int lane) {
   Rows A, B;
   bool vA = false, vB = false;
   {
-    const int32_t s0A = slot_at(0, rowA), s0B = slot_at(0, kOwn * cr + rowB);
-    const int32_t s1A = slot_at(1, rowA), s1B = slot_at(1, kOwn * cr + rowB);
+    const int32_t s0 = slot_at(0), s1 = slot_at(1);
     if constexpr (kPaged) {
-      fA = slot_fetch(a, c.req, raw_at(2, rowA));
-      fB = slot_fetch(a, c.req, raw_at(2, kOwn * cr + rowB));
-      nA = raw_at(3, rowA);
-      nB = raw_at(3, kOwn * cr + rowB);
+      fI = slot_fetch(a, c.req, raw_at(2));
+      nI = raw_at(3);
     } else {
-      nA = slot_at(2, rowA);
-      nB = slot_at(2, kOwn * cr + rowB);
+      nI = slot_at(2);
     }
+    int32_t s0A, s0B, s1A, s1B;
+    share(s0, s0A, s0B);
+    share(s1, s1A, s1B);
     if (c.ntiles > 0) load(s0A, s0B, A, vA);
     if (c.ntiles > 1) load(s1A, s1B, B, vB);
   }
