@@ -427,6 +427,33 @@ def test_paged_decode_with_non_power_of_two_pages(cuda_device, H):
     assert torch.equal(fused, flat) and torch.equal(fused_lse, flat_lse)
 
 
+@pytest.mark.parametrize("next_n,H", [(2, 64), (3, 16)])
+def test_shared_topk_equals_per_token_decode(cuda_device, next_n, H):
+    """next_n query tokens of a request sharing one top-k row, decoded as one
+    head group, give the per-token decode's result (each index row repeated)."""
+    from vllm_fp8kv.fp8_ds_mla_sparse_decode import fp8_ds_mla_sparse_decode_shared_topk
+
+    B, topk = 4, 512
+    s = synthetic.Shape("mtp", B=B, H=H, topk=topk, ctx=2048, pool_slots=B * 2048, mask_frac=0.1)
+    w = synthetic.make_host(s, seed=next_n + H)
+    pool = U.device_pool(w.kv_src_bits, check_against_oracle=False)
+    q = torch.randn((B, next_n, H, 576), generator=torch.Generator().manual_seed(H)).bfloat16().cuda()
+    idx = torch.from_numpy(w.slots).cuda()
+    out, lse = fp8_ds_mla_sparse_decode_shared_topk(q, pool, idx, w.sm_scale, return_lse=True,
+                                                    num_kv_splits=1)
+    per_tok, per_lse = fp8_ds_mla_sparse_decode(q.view(B * next_n, H, 576), pool,
+                                                idx.repeat_interleave(next_n, dim=0), w.sm_scale,
+                                                return_lse=True, num_kv_splits=1)
+    torch.cuda.synchronize()
+    U.assert_close(out.float().cpu().numpy().reshape(B * next_n, H, 512),
+                   per_tok.float().cpu().numpy())
+    U.assert_lse_close(lse.cpu().numpy().reshape(B * next_n, H), per_lse.cpu().numpy())
+    ref, ref_lse = O.sparse_decode(q.float().cpu().numpy().reshape(B * next_n, H, 576),
+                                   pool.view(-1, 656).cpu().numpy(),
+                                   np.repeat(w.slots, next_n, axis=0), w.sm_scale)
+    U.assert_close(out.float().cpu().numpy().reshape(B * next_n, H, 512), ref)
+
+
 def test_paged_decode_rejects_bad_tables(cuda_device):
     from vllm_fp8kv.fp8_ds_mla_sparse_decode import fp8_ds_mla_sparse_decode_paged
 

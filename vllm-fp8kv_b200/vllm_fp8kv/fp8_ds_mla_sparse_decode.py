@@ -200,3 +200,41 @@ def fp8_ds_mla_sparse_decode_paged(
         splits, ws_ptr, ws_bytes, N.stream_ptr(q.device))
     N.check(rc, "fp8_ds_mla_sparse_decode_paged")
     return (out, lse) if return_lse else out
+
+
+def fp8_ds_mla_sparse_decode_shared_topk(
+    q: torch.Tensor,          # [batch, next_n, h_q, 576] bf16: next_n query tokens per request
+    kv_cache: torch.Tensor,   # [..., 656] uint8 or float8_e4m3fn, contiguous
+    indices: torch.Tensor,    # [batch, topk] or [batch, 1, topk] int32 flat slots; -1 = masked
+    sm_scale: float,
+    return_lse: bool = False,
+    *,
+    num_kv_splits: int | None = None,
+    workspace: torch.Tensor | None = None,
+):
+    """Decode for requests whose next_n query tokens (multi-token prediction,
+    speculative drafts) attend to one shared top-k set.
+
+    Equal to `fp8_ds_mla_sparse_decode` over q.view(batch * next_n, h_q, 576)
+    with each request's index row repeated next_n times, because every
+    (query token, head) row is computed independently.  Here a request's
+    next_n * h_q query heads form one head group of one call: its rows are
+    gathered once instead of next_n times, and 64-head models with next_n = 2
+    fill the 128-row tile of the paired tensor-core kernel instead of padding
+    it.  No reference counterpart (the reference decodes one query token per
+    index row).  Returns out [batch, next_n, h_q, 512] (and lse
+    [batch, next_n, h_q]).
+    """
+    assert q.dim() == 4, "q must be [batch, next_n, h_q, 576]"
+    B, n, H, D = q.shape
+    assert indices.dim() == 2 or (indices.dim() == 3 and indices.shape[1] == 1), \
+        "indices must be [batch, topk] (one kv group shared by the next_n tokens)"
+    assert indices.shape[0] == B, "one index row per request"
+    assert q.stride(1) == H * q.stride(2), "q's next_n and head dims must be mergeable"
+    qv = q.view(B, n * H, D)
+    res = fp8_ds_mla_sparse_decode(qv, kv_cache, indices, sm_scale, return_lse,
+                                   num_kv_splits=num_kv_splits, workspace=workspace)
+    if return_lse:
+        out, lse = res
+        return out.view(B, n, H, out.shape[-1]), lse.view(B, n, H)
+    return res.view(B, n, H, res.shape[-1])
