@@ -220,6 +220,13 @@ __device__ void producer(const DecodeArgs& a, Smem& s, const CUtensorMap* tm, in
     }
   }
   cp_async_wait<0>();  // no index copy may outlive the CTA
+  // nor a TMA copy: the last stages and Q buffers have landed before the
+  // producer returns, even if a consumer's wait timed out (in a normal run
+  // these phases completed long ago and the waits return at once)
+  for (int x = g > kRawStages ? g - kRawStages : 0; x < g; ++x)
+    (void)warp_wait(smem_u32(&s.raw_full[x % kRawStages]), (x / kRawStages) & 1, 26);
+  for (int x = qc > kQBufs ? qc - kQBufs : 0; x < qc; ++x)
+    (void)warp_wait(smem_u32(&s.q_full[x % kQBufs]), (x / kQBufs) & 1, 27);
 }
 
 // ------------------------------------------------------------------ dequant (warps 1-8)
