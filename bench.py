@@ -14,10 +14,11 @@ e2e        = same metric through the public Python API with the step's q and
              indices copied from pinned host memory and out copied back, each
              direction on its own stream (double-buffered) so step i's copies
              overlap the decode of its neighbours, as a serving loop runs
-roofline   = the decode kernel's achieved TFLOP/s (or GB/s for the HBM-bound
-             shapes) from CUDA events around each launch on its stream, taken
-             in a second pass after the reported back-to-back window, against
-             MEASURED_PEAKS.json
+roofline   = the decode call's achieved TFLOP/s (or GB/s for the HBM-bound
+             shapes) over the same back-to-back window as ms_per_step (CUDA
+             events on the launching stream; a split call's time includes its
+             merge launch), against MEASURED_PEAKS.json; launch_us (events
+             around each call, a second pass) is reported beside it
 cpu_baseline = the oracle's numpy restatement of the reference's fp32 torch
              golden path, on a bounded sample of the same workload, rank 0, N=1
 --impl reference = that CPU implementation alone, as the reference arm
@@ -60,7 +61,7 @@ class ClockSampler:
         0x100: "display_clock_setting",
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.002):
+    def __init__(self, device_index: int, period_s: float = 0.001):
         self.samples, self.reasons = [], 0
         self.period = period_s
         self._stop = threading.Event()
@@ -163,6 +164,18 @@ def shard_seeds(rank: int) -> tuple[int, int]:
     return 1000 + rank, 2000 + rank
 
 
+def gather_ranks(value, dist, device) -> list[float]:
+    """Every rank's `value`, in rank order (after the timed regions)."""
+    import torch
+
+    if dist is None:
+        return [float(value)]
+    world = dist.get_world_size()
+    out = [torch.zeros(1, dtype=torch.float64, device=device) for _ in range(world)]
+    dist.all_gather(out, torch.tensor([float(value)], dtype=torch.float64, device=device))
+    return [float(t.item()) for t in out]
+
+
 def max_over_ranks(values, dist, device) -> list[float]:
     """Element-wise max of per-rank timings, on every rank (the slowest rank
     sets the job's step time).  `dist` is torch.distributed or None for one
@@ -261,6 +274,11 @@ def run_ours(args, rank, world, local_rank):
                                         num_kv_splits=splits, workspace=ws)
 
     stream = torch.cuda.current_stream(dev)
+    # clocks are sampled over the whole GPU phase (warm-up, the timed window,
+    # the per-launch pass and the end-to-end pass): the timed window alone is
+    # a few milliseconds
+    clk = ClockSampler(dev.index if dev.index is not None else 0)
+    clk.__enter__()
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
@@ -272,12 +290,11 @@ def run_ours(args, rank, world, local_rank):
     if dist:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
-        w0.record(stream)
-        for i in range(args.steps):
-            step(i)
-        w1.record(stream)
-        torch.cuda.synchronize(dev)
+    w0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    w1.record(stream)
+    torch.cuda.synchronize(dev)
     if dist:
         dist.barrier()
     window_ms = w0.elapsed_time(w1)
@@ -353,10 +370,12 @@ def run_ours(args, rank, world, local_rank):
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1) / args.steps
+    clk.__exit__(None, None, None)
     h2d_b = sets[0][0].numel() * 2 + sets[0][1].numel() * 4
     d2h_b = hout[0].numel() * 2 + hlse[0].numel() * 4
 
     # ---- max over ranks (no collective on the hot path; this is after timing)
+    per_rank_ms = gather_ranks(step_ms, dist, dev)
     step_ms, e2e_ms, launch_ms = max_over_ranks([step_ms, e2e_ms, launch_ms], dist, dev)
 
     from vllm_fp8kv.fp8_ds_mla_sparse_decode import decode_kernel_name
@@ -371,18 +390,23 @@ def run_ours(args, rank, world, local_rank):
         alg = synthetic.algorithmic_bytes(s.B, s.H, s.topk)
         peaks = _peaks()
         tensor_bound = s.H >= 64
+        # the call's time in the reported back-to-back window (all of its
+        # launches: a split call's merge is inside it)
         if tensor_bound:
-            achieved = flops / (launch_ms * 1e-3) / 1e12
+            achieved = flops / (step_ms * 1e-3) / 1e12
             peak = peaks["bf16_tflops"]
             roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                     "frac": achieved / peak}
         else:
-            achieved = alg / (launch_ms * 1e-3) / 1e9
+            achieved = alg / (step_ms * 1e-3) / 1e9
             peak = peaks["hbm_gbs"]
             roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                     "frac": achieved / peak}
         roof["peak_source"] = peaks["source"] + " (burst)"
         roof["kernel"] = kern
+        roof["time_source"] = ("back-to-back window = ms_per_step"
+                               + (" (decode + merge launches)" if launches_per_step > 1 else ""))
+        roof["kernel_us"] = step_ms * 1e3
         roof["launch_us"] = launch_ms * 1e3
         roof["traffic"] = _traffic_per_launch(kern, args.workload)
         roof["algorithmic_bytes_per_launch"] = alg
@@ -410,6 +434,8 @@ def run_ours(args, rank, world, local_rank):
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clk.summary(),
         }
+        if world > 1:
+            line["per_rank_us"] = [round(v * 1e3, 2) for v in per_rank_ms]
     if dist:
         dist.barrier()
         dist.destroy_process_group()

@@ -85,6 +85,20 @@ FP8MLA_API uint32_t fp8mla_wait_limit(void);
 FP8MLA_API int fp8mla_selftest_wait_timeout(uint32_t iters, uint64_t* elapsed_ns, void* stream);
 
 /*
+ * Lowers the limit of the hand-off waits of the small-head decode kernel
+ * (decode_ws_kernel: raw rows, key rows and Q between its producer, dequant
+ * and compute warps) to `iters` try_wait calls for the decode calls that
+ * follow in this process; 0 restores fp8mla_wait_limit().  With a limit of a
+ * few calls the waits give up while the copies they wait for are still
+ * arriving, so a test can drive the kernel's error path without a fault:
+ * the producer stops issuing copies, waits (with the full limit) for those it
+ * issued, every warp returns, and the status word carries the timeout.
+ * Results of such calls are meaningless.  For tests; no reference
+ * counterpart.  Returns FP8MLA_ERR_INVALID_ARGUMENT above the full limit.
+ */
+FP8MLA_API int fp8mla_selftest_set_wait_limit(uint32_t iters);
+
+/*
  * Split-KV count the decode picks when called with num_splits = 0.
  * Replaces the host heuristic `_choose_num_kv_splits`
  * (tests/fixtures/triton_mla_sparse_kernel_pr47629.py:406-423): a power of two

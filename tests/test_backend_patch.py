@@ -147,3 +147,25 @@ def test_forward_mqa_dispatch_and_fused_index_conversion(vllm, cuda_device):
     assert slots[0, :4].tolist() == [3 * 64, 3 * 64 + 1, 64, -1]
     flat = backend_patch._forward_fp8_kv(impl, q, pool, slots, attn_metadata=None)
     assert torch.equal(out, flat)
+
+
+@pytest.mark.parametrize("width,topk_tokens", [(256, 128), (128, 256), (192, 192)])
+def test_fused_paged_path_keeps_the_converter_contract(vllm, width, topk_tokens):
+    """The fp8 path converts inside the decode, so it must refuse what vLLM's
+    converter refuses: a top-k buffer whose width is not attn_metadata.topk_tokens,
+    and a topk_tokens that is not a multiple of the converter's 128-entry block
+    (reference backend_patch.py:83-89).  Checked before any device work."""
+    backend_patch.apply()
+
+    class Md:
+        req_id_per_token = torch.zeros(1, dtype=torch.int32)
+        block_table = torch.zeros((1, 8), dtype=torch.int32)
+        block_size = 64
+
+    Md.topk_tokens = topk_tokens
+    impl = vllm.impl(kv_cache_dtype="fp8_ds_mla", softmax_scale=1 / 24.0)
+    impl.topk_indices_buffer = torch.zeros((1, width), dtype=torch.int32)
+    q = torch.zeros(1, 16, NOPE + ROPE, dtype=torch.bfloat16)
+    pool = torch.zeros(8, 64, 656, dtype=torch.uint8)
+    with pytest.raises(AssertionError):
+        impl.forward_mqa(q, pool, Md, None)

@@ -60,3 +60,37 @@ def test_selftest_rejects_iteration_counts_outside_the_limit(cuda_device):
     assert L.fp8mla_selftest_wait_timeout(0, ctypes.byref(ns), None) == N.ERR_INVALID_ARGUMENT
     assert L.fp8mla_selftest_wait_timeout(L.fp8mla_wait_limit() + 1, ctypes.byref(ns),
                                           None) == N.ERR_INVALID_ARGUMENT
+
+
+def test_small_head_decode_timeout_path_returns_and_reports(cuda_device):
+    """Drive decode_ws_kernel's own error path: with a hand-off limit of two
+    try_wait calls its waits give up while rows are still arriving.  The
+    producer then stops issuing copies, waits for the ones it issued, and every
+    warp returns: the call completes, the status word carries the timeout bit
+    with the small-head kernel's wait codes (20-27, OR-ed together when several
+    waits gave up, so within [16, 32)), and after restoring the limit the same
+    context decodes correctly."""
+    L = N.lib()
+    s = synthetic.Shape("fdws", B=16, H=16, topk=1024, ctx=4096, pool_slots=16 * 4096,
+                        mask_frac=0.1)
+    w = synthetic.make_host(s, seed=21)
+    pool = U.device_pool(w.kv_src_bits, check_against_oracle=False)
+    q = U.bf16_tensor(w.q_bits)
+    idx = torch.from_numpy(w.slots).cuda()
+    N.device_status(reset=True)
+    assert L.fp8mla_selftest_set_wait_limit(L.fp8mla_wait_limit() + 1) == N.ERR_INVALID_ARGUMENT
+    N.check(L.fp8mla_selftest_set_wait_limit(2), "set wait limit")
+    try:
+        fp8_ds_mla_sparse_decode(q, pool, idx, w.sm_scale, num_kv_splits=2)
+        torch.cuda.synchronize()
+        st = N.device_status(reset=True)
+    finally:
+        N.check(L.fp8mla_selftest_set_wait_limit(0), "restore wait limit")
+    assert st & 1, f"no timeout recorded (status {st:#x})"
+    assert 16 <= (st >> 8) < 32, f"unexpected wait code in status {st:#x}"
+    out, lse = fp8_ds_mla_sparse_decode(q, pool, idx, w.sm_scale, return_lse=True, num_kv_splits=2)
+    ref, ref_lse = O.sparse_decode(synthetic.bf16_to_f32(w.q_bits), pool.view(-1, 656).cpu().numpy(),
+                                   w.slots, w.sm_scale)
+    U.assert_close(out.float().cpu().numpy(), ref)
+    U.assert_lse_close(lse.cpu().numpy(), ref_lse)
+    assert N.device_status(reset=True) == 0

@@ -41,9 +41,10 @@ def _rank_main(rank, world, port, q):
     try:
         # rank r timed [1 + r, 10 - r, 5]: every rank must see the max of each
         got = bench.max_over_ranks([1.0 + rank, 10.0 - rank, 5.0], dist, "cpu")
+        per_rank = bench.gather_ranks(0.5 + rank, dist, "cpu")
         seeds = bench.shard_seeds(rank)
         ref_line = bench.run_reference_arm(None, rank) if rank != 0 else "rank0"
-        q.put((rank, got, seeds, ref_line))
+        q.put((rank, got, seeds, ref_line, per_rank))
     finally:
         dist.barrier()
         dist.destroy_process_group()
@@ -60,9 +61,10 @@ def test_two_gloo_ranks_take_the_max_and_shard_their_data():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    by_rank = {r: (got, seeds, ref) for r, got, seeds, ref in results}
+    by_rank = {r: (got, seeds, ref, per) for r, got, seeds, ref, per in results}
     for r in range(world):
         assert by_rank[r][0] == [2.0, 10.0, 5.0]          # max over ranks, on every rank
+        assert by_rank[r][3] == [0.5, 1.5]                # every rank's step time, rank order
     assert by_rank[0][1] != by_rank[1][1]                  # each rank its own pool and sets
     assert by_rank[1][2] is None                           # reference arm: rank 1 does no work
 

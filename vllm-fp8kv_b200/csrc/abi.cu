@@ -5,6 +5,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -29,6 +30,9 @@ int check_cuda(cudaError_t e, const char* what) {
 }
 
 namespace {
+// Hand-off wait limit of the small-head kernel (fp8mla_selftest_set_wait_limit).
+std::atomic<uint32_t> g_handoff_wait_iters{kMaxWaitIters};
+
 constexpr int kMaxDevices = 64;
 struct DevInfo {
   int sms = 0, major = 0, minor = 0;
@@ -93,11 +97,15 @@ int auto_splits(int64_t T, int64_t H, int64_t G, int64_t topk, bool pair_kernel,
 }
 bool pair_heads(int64_t H, int64_t G) { return G > 0 && (H / G == 128 || H / G == 64); }
 
-int64_t ws_bytes(int64_t T, int64_t H, int S) {
+// Split workspace: the normalised partials ws_o[T][H][S][512] (elem_bytes
+// each: 2 when the output is bf16, 4 when it is fp32), padded to 256 bytes,
+// then the split LSEs ws_lse[T][H][S] (fp32).
+int64_t ws_o_bytes(int64_t T, int64_t H, int S, int elem_bytes) {
+  return ((T * H * S * kNope * elem_bytes + 255) / 256) * 256;
+}
+int64_t ws_bytes(int64_t T, int64_t H, int S, int elem_bytes) {
   if (S <= 1) return 0;
-  const int64_t o = T * H * S * kNope * 4;
-  const int64_t l = T * H * S * 4;
-  return ((o + 255) / 256) * 256 + l;
+  return ws_o_bytes(T, H, S, elem_bytes) + T * H * S * 4;
 }
 }  // namespace
 
@@ -139,6 +147,14 @@ int fp8mla_selftest_wait_timeout(uint32_t iters, uint64_t* elapsed_ns, void* str
 
 uint32_t fp8mla_wait_limit(void) { return kMaxWaitIters; }
 
+int fp8mla_selftest_set_wait_limit(uint32_t iters) {
+  g_last_error[0] = 0;
+  if (iters > kMaxWaitIters)
+    return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "iters must be in [0, %u]", kMaxWaitIters);
+  g_handoff_wait_iters.store(iters == 0 ? kMaxWaitIters : iters);
+  return FP8MLA_OK;
+}
+
 int fp8mla_choose_num_splits(int64_t T, int64_t H, int64_t G, int64_t topk, int sm_count) {
   if (G <= 0 || H <= 0 || H % G != 0) return 1;
   return pick_splits(T, H, G, topk, sm_count);
@@ -152,7 +168,9 @@ int64_t fp8mla_decode_workspace_bytes(int64_t T, int64_t H, int64_t G, int64_t t
     num_splits = auto_splits(T, H, G, topk, pair_heads(H, G), device_sm_count());
   }
   if (num_splits > 64) num_splits = 64;
-  return ws_bytes(T, H, num_splits);
+  // sized for fp32 partials: an upper bound for bf16 outputs (their partials
+  // are bf16)
+  return ws_bytes(T, H, num_splits, 4);
 }
 
 const char* fp8mla_decode_kernel_name(int64_t T, int64_t H, int64_t G, int64_t topk, int q_dtype,
@@ -256,15 +274,16 @@ int decode_impl(const void* q, int q_dtype, int64_t T, int64_t H, int64_t q_stri
   a.lse_st = lse_stride_t;
   a.num_splits = S;
   a.split_len = (int)((topk + S - 1) / S);
+  a.wait_iters = g_handoff_wait_iters.load();
   if (S > 1) {
-    const int64_t need = ws_bytes(T, H, S);
+    const int elem = q_dtype == FP8MLA_DTYPE_BF16 ? 2 : 4;  // partials in the output dtype
+    const int64_t need = ws_bytes(T, H, S, elem);
     if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
       return set_error(FP8MLA_ERR_WORKSPACE,
                        "split-KV with %d splits needs %lld bytes of 16-B aligned workspace, got %lld",
                        S, (long long)need, (long long)workspace_bytes);
     a.ws_o = static_cast<float*>(workspace);
-    a.ws_lse = reinterpret_cast<float*>(static_cast<char*>(workspace) +
-                                        ((T * H * S * kNope * 4 + 255) / 256) * 256);
+    a.ws_lse = reinterpret_cast<float*>(static_cast<char*>(workspace) + ws_o_bytes(T, H, S, elem));
   }
   if (paged != nullptr) {
     a.req_id = paged->req_id;

@@ -17,6 +17,8 @@
 // the GPU (different streams, or other threads) race on it and must be
 // serialised by the caller.  The split kernels overwrite every workspace entry
 // the merge reads, so nothing has to be cleared between calls.
+#include <stdio.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -55,22 +57,26 @@ extern "C" int fp8mla_sparse_decode_noalloc(
     const uint8_t* kv, int64_t num_slots, const int32_t* indices, int64_t G, int64_t topk,
     int64_t idx_stride_t, int64_t idx_stride_g, float sm_scale, void* out, int64_t out_stride_t,
     int64_t out_stride_h, float* lse, int64_t lse_stride_t, int num_splits, void* stream) {
-  if (G > 0 && H > 0 && H % G == 0 && T > 0) {
-    const int64_t need = fp8mla_decode_workspace_bytes(T, H, G, topk, num_splits);
-    if (need > kNoAllocScratchBytes)
-      return set_error(FP8MLA_ERR_WORKSPACE,
-                       "fp8mla_sparse_decode_noalloc: this shape needs %lld bytes of split-KV "
-                       "workspace, above the fixed %lld-byte scratch; use fewer splits or "
-                       "fp8mla_sparse_decode with a caller-provided workspace",
-                       (long long)need, (long long)kNoAllocScratchBytes);
-  }
   int dev = -1;
   void* scratch = scratch_for_current_device(&dev);
   if (scratch == nullptr)
     return set_error(FP8MLA_ERR_CUDA, "fp8mla_sparse_decode_noalloc: scratch lookup failed: %s",
                      dev >= 0 ? cudaGetErrorString(g_err[dev]) : "no current device");
-  return fp8mla_sparse_decode(q, q_dtype, T, H, q_stride_t, q_stride_h, kv, num_slots, indices, G,
-                              topk, idx_stride_t, idx_stride_g, sm_scale, out, out_stride_t,
-                              out_stride_h, lse, lse_stride_t, num_splits, scratch,
-                              kNoAllocScratchBytes, stream);
+  // The decode sizes the split workspace for the split count it actually
+  // runs (after its clamps) and refuses a call that needs more than it is
+  // given, before any launch; only the message is specific to this entry.
+  const int rc = fp8mla_sparse_decode(q, q_dtype, T, H, q_stride_t, q_stride_h, kv, num_slots,
+                                      indices, G, topk, idx_stride_t, idx_stride_g, sm_scale, out,
+                                      out_stride_t, out_stride_h, lse, lse_stride_t, num_splits,
+                                      scratch, kNoAllocScratchBytes, stream);
+  if (rc == FP8MLA_ERR_WORKSPACE) {
+    char why[400];
+    snprintf(why, sizeof(why), "%s", fp8mla_last_error());
+    return set_error(FP8MLA_ERR_WORKSPACE,
+                     "fp8mla_sparse_decode_noalloc: the split workspace does not fit the fixed "
+                     "%lld-byte scratch (%s); use fewer splits or fp8mla_sparse_decode with a "
+                     "caller-provided workspace",
+                     (long long)kNoAllocScratchBytes, why);
+  }
+  return rc;
 }

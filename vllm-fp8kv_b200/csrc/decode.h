@@ -37,6 +37,10 @@ struct DecodeArgs {
   int64_t max_blocks;
   int block_size;
   int block_shift;   // log2(block_size) when it is a power of two, else -1
+  // try_wait calls after which a hand-off wait of decode_ws_kernel gives up
+  // (the library default, lowered only by fp8mla_selftest_set_wait_limit);
+  // its drains before exit keep the full limit
+  uint32_t wait_iters;
 };
 
 #ifdef __CUDACC__

@@ -111,8 +111,9 @@ __device__ __forceinline__ Unit unit_of(const DecodeArgs& a, int u) {
 }
 
 // Bounded warp wait after which every lane has acquired the phase itself.
-__device__ __forceinline__ bool warp_acquire(uint32_t bar, uint32_t parity, uint32_t where) {
-  const bool ok = warp_wait(bar, parity, where);
+__device__ __forceinline__ bool warp_acquire(uint32_t bar, uint32_t parity, uint32_t where,
+                                             uint32_t iters) {
+  const bool ok = warp_wait_n(bar, parity, where, iters);
   if (ok) (void)mbar_try_wait(bar, parity);
   return ok;
 }
@@ -178,16 +179,22 @@ __device__ void producer(const DecodeArgs& a, Smem& s, const CUtensorMap* tm, in
 #pragma unroll 1
   for (int i = 0; i < kIdxAhead; ++i) fetch_idx(i);
 
+  // g: raw stages armed so far (chunk count), qc: Q buffers armed so far.
+  // A stage (buffer) is armed again only after its release was seen, which
+  // implies its previous copies landed; when a release wait gives up, the
+  // producer stops arming altogether.  So at the end only the last
+  // kRawStages stages and kQBufs buffers can still have copies in flight.
   int g = 0, qc = 0;
   bool ok = true;
-  for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+  for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
     const Unit x = unit_of(a, u);
     if (x.nch == 0) continue;
     const int32_t req = request_of(a, x.t);
-    // the unit's Q rows -> Q buffer qc & 1, once the compute warps are done with it
+    // the unit's Q rows -> the Q buffer, once the compute warps are done with it
     const int qb = qc % kQBufs;
     const uint32_t qfull = smem_u32(&s.q_full[qb]);
-    if (qc >= kQBufs && ok) ok = warp_wait(smem_u32(&s.q_empty[qb]), ((qc / kQBufs) + 1) & 1, 20);
+    if (qc >= kQBufs) ok = warp_wait_n(smem_u32(&s.q_empty[qb]), ((qc / kQBufs) + 1) & 1, 20, a.wait_iters);
+    if (!ok) break;
     if (lane == 0) mbar_arrive_expect_tx(qfull, (uint32_t)x.nh * kDqk * 2);
     __syncwarp();
     if (lane < x.nh)
@@ -195,7 +202,7 @@ __device__ void producer(const DecodeArgs& a, Smem& s, const CUtensorMap* tm, in
                     static_cast<const uint16_t*>(a.q) + x.t * a.q_st + (int64_t)(x.head0 + lane) * a.q_sh,
                     kDqk * 2, qfull);
     ++qc;
-    for (int c = 0; c < x.nch; ++c, ++g) {
+    for (int c = 0; c < x.nch; ++c) {
       // chunk g's indices (copy group g) have landed; lane i owns row i
       cp_async_wait<kIdxAhead - 1>();
       const int pos = x.beg + c * kBN + lane;
@@ -203,8 +210,9 @@ __device__ void producer(const DecodeArgs& a, Smem& s, const CUtensorMap* tm, in
       fetch_idx((g + kIdxAhead) % kIdxSlots);  // the slot read one chunk ago
       const int32_t slot = live_slot(a, req, raw);
       const int st = g % kRawStages;
-      if (g >= kRawStages && ok)
-        ok = warp_wait(smem_u32(&s.raw_empty[st]), ((g / kRawStages) + 1) & 1, 21);
+      if (g >= kRawStages)
+        ok = warp_wait_n(smem_u32(&s.raw_empty[st]), ((g / kRawStages) + 1) & 1, 21, a.wait_iters);
+      if (!ok) break;
       s.valid[st][lane] = slot >= 0 ? 1 : 0;
       const int32_t row = slot >= 0 ? slot : 0;  // masked: a valid row, flagged invalid
       const uint32_t bar = smem_u32(&s.raw_full[st]);
@@ -217,12 +225,14 @@ __device__ void producer(const DecodeArgs& a, Smem& s, const CUtensorMap* tm, in
       const int32_t r2 = __shfl_sync(0xFFFFFFFFu, row, (4 * lane + 2) & 31);
       const int32_t r3 = __shfl_sync(0xFFFFFFFFu, row, (4 * lane + 3) & 31);
       if (lane < 8) gather4(smem_u32(&s.raw[st][lane * kGroupBytes]), tm, r0, r1, r2, r3, bar);
+      ++g;
     }
   }
   cp_async_wait<0>();  // no index copy may outlive the CTA
-  // nor a TMA copy: the last stages and Q buffers have landed before the
-  // producer returns, even if a consumer's wait timed out (in a normal run
-  // these phases completed long ago and the waits return at once)
+  // nor a TMA copy: the stages and Q buffers armed last have landed before the
+  // producer returns, even after a timed-out wait (in a normal run these
+  // phases completed long ago and the waits return at once).  These waits
+  // keep the full limit whatever the hand-off limit is.
   for (int x = g > kRawStages ? g - kRawStages : 0; x < g; ++x)
     (void)warp_wait(smem_u32(&s.raw_full[x % kRawStages]), (x / kRawStages) & 1, 26);
   for (int x = qc > kQBufs ? qc - kQBufs : 0; x < qc; ++x)
@@ -237,7 +247,7 @@ __device__ void dequant(const DecodeArgs& a, Smem& s, int nunits, int dw, int la
     const int nch = unit_of(a, u).nch;
     for (int c = 0; c < nch; ++c, ++g) {
       const int st = g % kRawStages, ks = g % kKStages;
-      if (ok) ok = warp_acquire(smem_u32(&s.raw_full[st]), (g / kRawStages) & 1, 22);
+      if (ok) ok = warp_acquire(smem_u32(&s.raw_full[st]), (g / kRawStages) & 1, 22, a.wait_iters);
       const uint8_t* rs = s.raw[st];
       uint8_t* kst = reinterpret_cast<uint8_t*>(s.k[ks]);
       // all of this warp's rows are loaded before any is converted, so their
@@ -267,7 +277,7 @@ __device__ void dequant(const DecodeArgs& a, Smem& s, int nunits, int dw, int la
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&s.raw_empty[st]));
       if (g >= kKStages && ok)
-        ok = warp_wait(smem_u32(&s.k_empty[ks]), ((g / kKStages) + 1) & 1, 23);
+        ok = warp_wait_n(smem_u32(&s.k_empty[ks]), ((g / kKStages) + 1) & 1, 23, a.wait_iters);
 #pragma unroll
       for (int i = 0; i < kRowsPerDequantWarp; ++i) {
         const int r = dw + kDequantWarps * i;
@@ -318,7 +328,7 @@ __device__ void compute(const DecodeArgs& a, Smem& s, int nunits, int cw, int la
     float m_run = -INFINITY, l_run = 0.f;   // head sh (shared by its 16 threads)
     if (x.nch > 0) {
       const int qb = qc % kQBufs;
-      if (ok) ok = warp_acquire(smem_u32(&s.q_full[qb]), (qc / kQBufs) & 1, 24);
+      if (ok) ok = warp_acquire(smem_u32(&s.q_full[qb]), (qc / kQBufs) & 1, 24, a.wait_iters);
       uint32_t qf[kPartSteps][4];
       {
         const uint32_t qa0 = smem_u32(s.q[qb]) + (((lane & 15) * kKStride + (lane >> 4) * 8) << 1);
@@ -331,7 +341,7 @@ __device__ void compute(const DecodeArgs& a, Smem& s, int nunits, int cw, int la
       ++qc;
       for (int c = 0; c < x.nch; ++c, ++g) {
         const int ks = g % kKStages;
-        if (ok) ok = warp_acquire(smem_u32(&s.k_full[ks]), (g / kKStages) & 1, 25);
+        if (ok) ok = warp_acquire(smem_u32(&s.k_full[ks]), (g / kKStages) & 1, 25, a.wait_iters);
         const uint32_t k_base = smem_u32(s.k[ks]);
         // ---- partial S: two n8 tiles (tokens n0..n0+15) over this warp's k-steps
         float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};

@@ -29,6 +29,7 @@ SIGNATURES = {
     "fp8mla_device_status": (_I32, [ctypes.POINTER(ctypes.c_uint), _I32, _P]),
     "fp8mla_selftest_wait_timeout": (_I32, [ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint64), _P]),
     "fp8mla_wait_limit": (ctypes.c_uint32, []),
+    "fp8mla_selftest_set_wait_limit": (_I32, [ctypes.c_uint32]),
     "fp8mla_choose_num_splits": (_I32, [_I64, _I64, _I64, _I64, _I32]),
     "fp8mla_decode_workspace_bytes": (_I64, [_I64, _I64, _I64, _I64, _I32]),
     "fp8mla_decode_kernel_name": (ctypes.c_char_p, [_I64, _I64, _I64, _I64, _I32, _I32]),
@@ -107,7 +108,20 @@ def stream_ptr(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-def require_cuda(*tensors) -> None:
+def require_cuda(*tensors):
+    """Check that every tensor is a CUDA tensor on one device; return that device.
+
+    The library reads the SM count, the per-device set-up and the launch
+    device from the CUDA current device, so callers run it under
+    ``torch.cuda.device(<this device>)`` with the stream of this device."""
+    dev = None
     for t in tensors:
-        if t is not None and not t.is_cuda:
+        if t is None:
+            continue
+        if not t.is_cuda:
             raise Fp8MlaError("libfp8mla kernels need CUDA tensors (sm_100); there is no CPU path")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise AssertionError(f"all tensors must be on one device: {dev} and {t.device}")
+    return dev

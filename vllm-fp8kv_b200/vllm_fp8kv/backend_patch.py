@@ -27,6 +27,7 @@ from vllm_fp8kv.fp8_ds_mla_sparse_decode import (
 FP8_DS_MLA = "fp8_ds_mla"
 _CLI_FP8_NAMES = ("fp8", "fp8_e4m3")
 _MARK = "_vllm_fp8kv_b200"
+_CONVERT_BLOCK_N = 128  # entries per program of vLLM's index converter
 
 
 def _as_single_q(q):
@@ -52,6 +53,15 @@ def _forward_fp8_kv_paged(self, q, kv_c_and_k_pe_cache, topk_indices, attn_metad
     q = _as_single_q(q)
     n_tok = q.shape[0]
     md = attn_metadata
+    # the converter's contract (vLLM sparse_utils.py, called with
+    # NUM_TOPK_TOKENS=attn_metadata.topk_tokens at the reference's
+    # backend_patch.py:83-89): the buffer row is exactly topk_tokens wide and
+    # topk_tokens is a multiple of its 128-entry block
+    width = topk_indices.shape[-1]
+    assert width == md.topk_tokens, (
+        f"topk_indices_buffer width {width} != attn_metadata.topk_tokens {md.topk_tokens}")
+    assert md.topk_tokens % _CONVERT_BLOCK_N == 0, (
+        f"NUM_TOPK_TOKENS ({md.topk_tokens}) must be divisible by BLOCK_N ({_CONVERT_BLOCK_N})")
     out = fp8_ds_mla_sparse_decode_paged(
         q, kv_c_and_k_pe_cache, md.req_id_per_token[:n_tok].to(torch.int32).contiguous(),
         md.block_table.to(torch.int32), topk_indices.view(n_tok, 1, -1),

@@ -29,13 +29,14 @@ def concat_and_cache_ds_mla(kv_c: torch.Tensor, k_pe: torch.Tensor, kv_cache: to
     assert kv_c.shape[0] == k_pe.shape[0] == slot_mapping.shape[0]
     assert kv_cache.dtype in (torch.uint8, torch.float8_e4m3fn) and kv_cache.is_contiguous()
     assert kv_cache.shape[-1] == ROW_BYTES, "fp8_ds_mla rows are 656 bytes"
-    N.require_cuda(kv_c, k_pe, kv_cache, slot_mapping)
+    dev = N.require_cuda(kv_c, k_pe, kv_cache, slot_mapping)
     slots = slot_mapping.to(torch.int64).contiguous()
     flat = kv_cache.view(torch.uint8).reshape(-1, ROW_BYTES)
-    rc = N.lib().fp8mla_ds_mla_write(
-        kv_c.data_ptr(), kv_c.stride(0), k_pe.data_ptr(), k_pe.stride(0),
-        slots.data_ptr(), slots.numel(), flat.data_ptr(), flat.shape[0],
-        N.stream_ptr(kv_c.device))
+    with torch.cuda.device(dev):
+        rc = N.lib().fp8mla_ds_mla_write(
+            kv_c.data_ptr(), kv_c.stride(0), k_pe.data_ptr(), k_pe.stride(0),
+            slots.data_ptr(), slots.numel(), flat.data_ptr(), flat.shape[0],
+            N.stream_ptr(dev))
     N.check(rc, "fp8mla_ds_mla_write")
 
 

@@ -26,20 +26,27 @@ import torch
 
 from vllm_fp8kv import _native as N
 
-FP16_NAN_MAG = 0x7F80
-
 _DT = {torch.float16: N.DTYPE_F16, torch.bfloat16: N.DTYPE_BF16, torch.float32: N.DTYPE_F32}
 
 
 def dequant_bitmath_torch(u8: torch.Tensor, dtype: torch.dtype = torch.float16) -> torch.Tensor:
-    """Torch bit-math decode: fp16((s << 15) | ((b & 0x7F) << 7)) * 256, NaN for 0x7F/0xFF."""
+    """Decode e4m3fn bytes from the format's definition, in integer/fp32 torch ops.
+
+    A byte is sign (bit 7), exponent e (bits 6..3, bias 7) and mantissa m
+    (bits 2..0): value = (-1)^s * 2^(e-7) * (1 + m/8) for e > 0, the subnormal
+    (-1)^s * 2^-6 * m/8 for e == 0, and NaN for e == 15, m == 7 (the format
+    has no infinities).  Every finite value is exact in fp16, bf16 and fp32,
+    so this equals torch's float8_e4m3fn cast (NaN payloads aside).
+    Same result as the reference's helper (vllm_fp8kv/fp8_dequant.py:47-58).
+    """
     assert u8.dtype == torch.uint8
-    b = u8.to(torch.int16)
-    sign = (b & 0x80) << 8
-    h = (sign | ((b & 0x7F) << 7)).view(torch.float16) * 256.0
-    nan = (sign | FP16_NAN_MAG).view(torch.float16)
-    out = torch.where((b & 0x7F) == 0x7F, nan, h)
-    return out if dtype == torch.float16 else out.to(dtype)
+    b = u8.to(torch.int32)
+    e = (b >> 3) & 0xF
+    m = (b & 0x7).to(torch.float32)
+    mag = torch.where(e == 0, m * 2.0 ** -9, torch.ldexp(1.0 + m / 8.0, e - 7))
+    val = torch.where((b & 0x80) != 0, -mag, mag)
+    val = torch.where((b & 0x7F) == 0x7F, torch.full_like(val, float("nan")), val)
+    return val.to(dtype)
 
 
 def build_lut(dtype: torch.dtype = torch.float16, device="cuda") -> torch.Tensor:
@@ -53,11 +60,12 @@ def dequant_device(u8: torch.Tensor, dtype: torch.dtype = torch.float16,
     """Decode a uint8 CUDA tensor of e4m3fn bytes with the sm_100a kernel."""
     assert u8.dtype == torch.uint8
     assert dtype in _DT, dtype
-    N.require_cuda(u8)
+    dev = N.require_cuda(u8)
     src = u8.contiguous().reshape(-1)
-    out = torch.empty(src.shape, dtype=dtype, device=u8.device)
-    rc = N.lib().fp8mla_dequant_e4m3(src.data_ptr(), src.numel(), out.data_ptr(), _DT[dtype],
-                                     method, N.stream_ptr(u8.device))
+    out = torch.empty(src.shape, dtype=dtype, device=dev)
+    with torch.cuda.device(dev):
+        rc = N.lib().fp8mla_dequant_e4m3(src.data_ptr(), src.numel(), out.data_ptr(), _DT[dtype],
+                                         method, N.stream_ptr(dev))
     N.check(rc, "fp8mla_dequant_e4m3")
     return out.reshape(u8.shape)
 
@@ -78,13 +86,14 @@ def dequant_ds_mla_rows(kv_cache: torch.Tensor, slots: torch.Tensor, method: int
     """
     assert method in (0, 1)
     assert slots.dtype == torch.int32 and slots.dim() == 1
-    N.require_cuda(kv_cache)
+    dev = N.require_cuda(kv_cache, slots)
     kv = kv_cache.view(torch.uint8) if kv_cache.dtype != torch.uint8 else kv_cache
     assert kv.is_contiguous() and kv.numel() % 656 == 0, "fp8_ds_mla pool must be contiguous"
     num_slots = kv.numel() // 656
     sl = slots.contiguous()
     out = torch.empty((sl.numel(), 576), dtype=torch.bfloat16, device=kv.device)
-    rc = N.lib().fp8mla_ds_mla_dequant_rows(kv.data_ptr(), num_slots, sl.data_ptr(), sl.numel(),
-                                            out.data_ptr(), 576, method, N.stream_ptr(kv.device))
+    with torch.cuda.device(dev):
+        rc = N.lib().fp8mla_ds_mla_dequant_rows(kv.data_ptr(), num_slots, sl.data_ptr(), sl.numel(),
+                                                out.data_ptr(), 576, method, N.stream_ptr(dev))
     N.check(rc, "fp8mla_ds_mla_dequant_rows")
     return out

@@ -2,17 +2,21 @@
 
 Drop-in for the reference entry point of the same name
 (vllm_fp8kv/fp8_ds_mla_sparse_decode.py:214-288): same signature, same
-asserts, same outputs.  The work runs in libfp8mla.so:
+asserts, same outputs.  The work runs in libfp8mla.so, which picks the
+kernel by head count and q dtype (``decode_kernel_name`` reports the choice):
 
-* H/G == 128 heads per kv group, bf16 q: the tcgen05/TMEM kernel (heads are
-  the MMA M dimension; QK^T over d=576 and PV over d_v=512 on the 5th-gen
-  tensor cores, accumulators in tensor memory);
-* any other head count: the split-KV warp-MMA kernel.
+* 64 or 128 heads per kv group, bf16 q: ``decode_tc2_kernel``, a 2-SM cluster
+  whose cta_group::2 tcgen05 MMAs take the heads as the M dimension (QK^T over
+  d=576 and PV over d_v=512, accumulators in tensor memory);
+* any other head count with bf16 q: ``decode_ws_kernel``, persistent and
+  warp-specialised, rows staged by TMA gather4;
+* fp32 q (the reference's CPU-test dtype): ``decode_mma_kernel``.
 
-Both gather 656-byte rows by flat slot with 64-bit offsets, issue no load for
-masked slots (index < 0 or >= num_slots), dequantize e4m3 * tile scale to
-bf16 exactly as the reference does, and merge top-k splits by LSE with no NaN
-on fully masked chunks.
+Split-KV calls add ``merge_splits_kernel``.  All of them gather 656-byte rows
+by flat slot with 64-bit offsets, issue no load for masked slots (index < 0
+or >= num_slots), dequantize e4m3 * tile scale to bf16 exactly as the
+reference does, and merge top-k splits by LSE with no NaN on fully masked
+chunks.
 
 fp8_ds_mla row (656 B/token):
     [  0:512)  512 x fp8e4m3   NoPE latent (kv_lora_rank)
@@ -93,7 +97,7 @@ def fp8_ds_mla_sparse_decode(
     kv_groups, topk = indices.shape[1], indices.shape[2]
     assert h_q % kv_groups == 0, f"h_q={h_q} not divisible by kv_groups={kv_groups}"
     assert indices.dtype == torch.int32, f"indices must be int32, got {indices.dtype}"
-    N.require_cuda(q, kv_u8, indices)
+    N.require_cuda(q, kv_u8, indices, workspace)
 
     # the kernels read q in 16-byte vectors; re-lay a misaligned view once
     vec = 8 if q.dtype == torch.bfloat16 else 4
@@ -112,15 +116,16 @@ def fp8_ds_mla_sparse_decode(
     ws_ptr = workspace.data_ptr() if (need and workspace is not None) else None
     ws_bytes = workspace.numel() * workspace.element_size() if (need and workspace is not None) else 0
 
-    rc = N.lib().fp8mla_sparse_decode(
-        q.data_ptr(), N.DTYPE_BF16 if q.dtype == torch.bfloat16 else N.DTYPE_F32,
-        seq_q, h_q, q.stride(0), q.stride(1),
-        kv_u8.data_ptr(), num_slots,
-        indices.data_ptr(), kv_groups, topk, indices.stride(0), indices.stride(1),
-        float(sm_scale),
-        out.data_ptr(), out.stride(0), out.stride(1),
-        lse.data_ptr() if lse is not None else None, lse.stride(0) if lse is not None else 0,
-        splits, ws_ptr, ws_bytes, N.stream_ptr(q.device))
+    with torch.cuda.device(q.device):
+        rc = N.lib().fp8mla_sparse_decode(
+            q.data_ptr(), N.DTYPE_BF16 if q.dtype == torch.bfloat16 else N.DTYPE_F32,
+            seq_q, h_q, q.stride(0), q.stride(1),
+            kv_u8.data_ptr(), num_slots,
+            indices.data_ptr(), kv_groups, topk, indices.stride(0), indices.stride(1),
+            float(sm_scale),
+            out.data_ptr(), out.stride(0), out.stride(1),
+            lse.data_ptr() if lse is not None else None, lse.stride(0) if lse is not None else 0,
+            splits, ws_ptr, ws_bytes, N.stream_ptr(q.device))
     N.check(rc, "fp8_ds_mla_sparse_decode")
     return (out, lse) if return_lse else out
 
@@ -168,7 +173,7 @@ def fp8_ds_mla_sparse_decode_paged(
         token_indices = token_indices.unsqueeze(1)
     kv_groups, topk = token_indices.shape[1], token_indices.shape[2]
     assert h_q % kv_groups == 0, f"h_q={h_q} not divisible by kv_groups={kv_groups}"
-    N.require_cuda(q, kv_u8, token_indices, req_id, block_table)
+    N.require_cuda(q, kv_u8, token_indices, req_id, block_table, workspace)
 
     vec = 8 if q.dtype == torch.bfloat16 else 4
     if q.data_ptr() % 16 or q.stride(0) % vec or q.stride(1) % vec:
@@ -186,18 +191,19 @@ def fp8_ds_mla_sparse_decode_paged(
     ws_ptr = workspace.data_ptr() if (need and workspace is not None) else None
     ws_bytes = workspace.numel() * workspace.element_size() if (need and workspace is not None) else 0
 
-    rc = N.lib().fp8mla_sparse_decode_paged(
-        q.data_ptr(), N.DTYPE_BF16 if q.dtype == torch.bfloat16 else N.DTYPE_F32,
-        seq_q, h_q, q.stride(0), q.stride(1),
-        kv_u8.data_ptr(), num_slots,
-        req_id.data_ptr(), block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
-        int(block_size),
-        token_indices.data_ptr(), kv_groups, topk, token_indices.stride(0),
-        token_indices.stride(1),
-        float(sm_scale),
-        out.data_ptr(), out.stride(0), out.stride(1),
-        lse.data_ptr() if lse is not None else None, lse.stride(0) if lse is not None else 0,
-        splits, ws_ptr, ws_bytes, N.stream_ptr(q.device))
+    with torch.cuda.device(q.device):
+        rc = N.lib().fp8mla_sparse_decode_paged(
+            q.data_ptr(), N.DTYPE_BF16 if q.dtype == torch.bfloat16 else N.DTYPE_F32,
+            seq_q, h_q, q.stride(0), q.stride(1),
+            kv_u8.data_ptr(), num_slots,
+            req_id.data_ptr(), block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
+            int(block_size),
+            token_indices.data_ptr(), kv_groups, topk, token_indices.stride(0),
+            token_indices.stride(1),
+            float(sm_scale),
+            out.data_ptr(), out.stride(0), out.stride(1),
+            lse.data_ptr() if lse is not None else None, lse.stride(0) if lse is not None else 0,
+            splits, ws_ptr, ws_bytes, N.stream_ptr(q.device))
     N.check(rc, "fp8_ds_mla_sparse_decode_paged")
     return (out, lse) if return_lse else out
 

@@ -26,15 +26,16 @@ def convert_req_index_to_global_index(req_id: torch.Tensor, block_table: torch.T
     assert token_indices.shape[1] == NUM_TOPK_TOKENS
     assert NUM_TOPK_TOKENS % BLOCK_N == 0, (
         f"NUM_TOPK_TOKENS ({NUM_TOPK_TOKENS}) must be divisible by BLOCK_N ({BLOCK_N})")
-    N.require_cuda(req_id, block_table, token_indices)
+    dev = N.require_cuda(req_id, block_table, token_indices, out)
     req = req_id.contiguous()
     bt = block_table.contiguous()
     ti = token_indices.contiguous()
     T = ti.shape[0]
     if out is None:
         out = torch.empty_like(ti)
-    rc = N.lib().fp8mla_convert_req_index(
-        req.data_ptr(), bt.data_ptr(), bt.stride(0), bt.shape[1], ti.data_ptr(), ti.stride(0),
-        T, NUM_TOPK_TOKENS, BLOCK_SIZE, out.data_ptr(), out.stride(0), N.stream_ptr(ti.device))
+    with torch.cuda.device(dev):
+        rc = N.lib().fp8mla_convert_req_index(
+            req.data_ptr(), bt.data_ptr(), bt.stride(0), bt.shape[1], ti.data_ptr(), ti.stride(0),
+            T, NUM_TOPK_TOKENS, BLOCK_SIZE, out.data_ptr(), out.stride(0), N.stream_ptr(dev))
     N.check(rc, "fp8mla_convert_req_index")
     return out
