@@ -247,6 +247,14 @@ def run_ours(args, rank, world, local_rank):
                                 device_id=dev)
 
     s = synthetic.SHAPES[args.workload]
+    if args.requests:
+        # a smaller case of the same workload (profiling captures): fewer
+        # requests; pools of disjoint contexts shrink with them
+        import dataclasses
+
+        pool = s.pool_slots if s.shared_pool else args.requests * s.ctx
+        s = dataclasses.replace(s, B=args.requests, pool_slots=pool,
+                                lead_masked_reqs=min(s.lead_masked_reqs, args.requests))
     pool_seed, set_seed = shard_seeds(rank)
     w = synthetic.make_device(s, seed=pool_seed, device=dev)
     splits = s.num_splits or None
@@ -449,6 +457,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5"])
+    ap.add_argument("--requests", type=int, default=0,
+                    help="per-GPU batch override for profiling a smaller case (0 = the workload's)")
     ap.add_argument("--cpu-sample", type=int, default=8,
                     help="requests in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
