@@ -34,6 +34,7 @@
 #include "common.cuh"
 #include "decode.h"
 #include "tc_ptx.cuh"
+#include "tma_map.h"
 
 namespace fp8mla {
 namespace ws {
@@ -121,15 +122,6 @@ __device__ __forceinline__ bool warp_acquire(uint32_t bar, uint32_t parity, uint
 // The compute warps' own barrier (id 1; the other warps never use it).
 __device__ __forceinline__ void named_sync_ws() {
   asm volatile("bar.sync 1, %0;\n" ::"n"(kComputeWarps * 32) : "memory");
-}
-
-__device__ __forceinline__ void gather4(uint32_t dst, const CUtensorMap* tm, int32_t r0, int32_t r1,
-                                        int32_t r2, int32_t r3, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cta.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];\n" ::"r"(dst),
-      "l"(tm), "r"(0), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
-      : "memory");
 }
 
 __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
@@ -224,7 +216,7 @@ __device__ void producer(const DecodeArgs& a, Smem& s, const CUtensorMap* tm, in
       const int32_t r1 = __shfl_sync(0xFFFFFFFFu, row, (4 * lane + 1) & 31);
       const int32_t r2 = __shfl_sync(0xFFFFFFFFu, row, (4 * lane + 2) & 31);
       const int32_t r3 = __shfl_sync(0xFFFFFFFFu, row, (4 * lane + 3) & 31);
-      if (lane < 8) gather4(smem_u32(&s.raw[st][lane * kGroupBytes]), tm, r0, r1, r2, r3, bar);
+      if (lane < 8) tma_gather4(smem_u32(&s.raw[st][lane * kGroupBytes]), tm, 0, r0, r1, r2, r3, bar);
       ++g;
     }
   }
@@ -521,19 +513,24 @@ EncodeTiledFn encode_fn() {
 }
 }  // namespace
 
-int launch_decode_ws(const DecodeArgs& a, int sms, cudaStream_t st) {
+int encode_row_map(CUtensorMap* tm, const uint8_t* kv, int64_t num_slots, uint32_t box_u64) {
   EncodeTiledFn enc = encode_fn();
   if (enc == nullptr) return set_error(FP8MLA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  // the pool as [num_slots] rows of 82 uint64: one gather4 box = 4 whole rows
-  CUtensorMap tm;
-  const cuuint64_t dims[2] = {kRowBytes / 8, (cuuint64_t)a.num_slots};
+  const cuuint64_t dims[2] = {kRowBytes / 8, (cuuint64_t)num_slots};
   const cuuint64_t strides[1] = {kRowBytes};
-  const cuuint32_t box[2] = {kRowBytes / 8, 1};
+  const cuuint32_t box[2] = {box_u64, 1};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(a.kv), dims, strides,
+  const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(kv), dims, strides,
                          box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(FP8MLA_ERR_CUDA, "tensor map encode failed (%d)", (int)r);
+  return FP8MLA_OK;
+}
+
+int launch_decode_ws(const DecodeArgs& a, int sms, cudaStream_t st) {
+  // the pool as [num_slots] rows of 82 uint64: one gather4 box = 4 whole rows
+  CUtensorMap tm;
+  if (int rc = encode_row_map(&tm, a.kv, a.num_slots, kRowBytes / 8)) return rc;
   const size_t smem = sizeof(ws::Smem) + 128;
   cudaError_t e = cudaFuncSetAttribute(ws::decode_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
