@@ -342,12 +342,12 @@ def test_no_on_chip_wait_timed_out(cuda_device):
 def test_dispatch_by_heads_and_dtype(cuda_device):
     from vllm_fp8kv.fp8_ds_mla_sparse_decode import decode_kernel_name
 
-    assert decode_kernel_name(64, 128, 1, 2048) == "decode_tc2_kernel"
-    assert decode_kernel_name(64, 256, 2, 2048) == "decode_tc2_kernel"
+    assert decode_kernel_name(64, 128, 1, 2048) == "decode_tc3_kernel"
+    assert decode_kernel_name(64, 256, 2, 2048) == "decode_tc3_kernel"
     # 64 heads per group run on the pair kernel too (the odd CTA's rows are
     # padding); 32 tokens x 1 group would fill 32 of 74 SM pairs, so the
     # automatic split count doubles to 2
-    assert decode_kernel_name(32, 64, 1, 2048) == "decode_tc2_kernel+merge_splits_kernel"
+    assert decode_kernel_name(32, 64, 1, 2048) == "decode_tc3_kernel+merge_splits_kernel"
     assert decode_kernel_name(64, 128, 1, 2048, torch.float32) == "decode_mma_kernel"
     # small head counts with bf16 q: the persistent TMA-gather kernel
     assert decode_kernel_name(256, 16, 1, 2048, torch.bfloat16, 8) == \

@@ -83,7 +83,7 @@ def c4_pool(cuda_device):
 
 @pytest.mark.parametrize("H", [128, 64])
 def test_pair_kernel_offsets_past_2_31_flat_and_paged(c4_pool, H):
-    """decode_tc2_kernel (64 and 128 heads) on the c4 pool: rows at
+    """decode_tc3_kernel (64 and 128 heads) on the c4 pool: rows at
     num_slots - 1, around slot 3,273,603 and spread above it; the paged entry
     point over a block table whose pages sit at the top of the pool gives the
     same bits as the flat one."""
@@ -94,7 +94,7 @@ def test_pair_kernel_offsets_past_2_31_flat_and_paged(c4_pool, H):
     B = 4
     slots = _place_past_boundary(w.slots[:B], n, rng)
     q = torch.randn((B, H, 576), generator=torch.Generator().manual_seed(H)).bfloat16().cuda()
-    assert decode_kernel_name(B, H, 1, 2048).startswith("decode_tc2_kernel")
+    assert decode_kernel_name(B, H, 1, 2048).startswith("decode_tc3_kernel")
     out, lse = fp8_ds_mla_sparse_decode(q, w.kv, slots, w.sm_scale, return_lse=True)
     _check_requests(out, lse, q, w.kv, slots, w.sm_scale, range(B))
 
@@ -158,7 +158,7 @@ def test_c4_full_shape_edges_a_b_at_the_north_star_tolerance(c4_pool):
     high = (w.slots > BOUNDARY_SLOT).float().mean().item()
     assert high > 0.1, high
     # two splits: the count the library picks for 32 pairs of this shape
-    assert decode_kernel_name(B, 64, 1, 2048) == "decode_tc2_kernel+merge_splits_kernel"
+    assert decode_kernel_name(B, 64, 1, 2048) == "decode_tc3_kernel+merge_splits_kernel"
     out, lse = fp8_ds_mla_sparse_decode(w.q, w.kv, w.slots, w.sm_scale, return_lse=True,
                                         num_kv_splits=2)
     _check_requests(out, lse, w.q, w.kv, w.slots, w.sm_scale, (0, 7, 8, 19, 31))
@@ -233,7 +233,7 @@ def test_c5_full_pool_subset(cuda_device):
         n = w.kv.view(-1, 656).shape[0]
         assert n == 8_388_608
         assert int(w.slots.max()) > 2 * BOUNDARY_SLOT
-        assert decode_kernel_name(128, 128, 1, 2048) == "decode_tc2_kernel"
+        assert decode_kernel_name(128, 128, 1, 2048) == "decode_tc3_kernel"
         out, lse = fp8_ds_mla_sparse_decode(w.q, w.kv, w.slots, w.sm_scale, return_lse=True)
         _check_requests(out, lse, w.q, w.kv, w.slots, w.sm_scale, (0, 45, 90, 127))
         for b in (17, 101):

@@ -1,6 +1,6 @@
 // decode_tc3.cu -- sparse MLA decode for 64 or 128 heads per kv group on a
-// pair of SMs (a 2-CTA cluster) sharing cta_group::2 tcgen05 MMAs, with the
-// selected rows staged in shared memory by TMA.
+// pair of SMs (a 2-CTA cluster) sharing cta_group::2 tcgen05 MMAs, with each
+// CTA's own rows staged in shared memory by TMA.
 //
 // The MMA side is decode_tc2.cu's: the pair splits the heads (CTA c owns
 // heads [64c, 64c+64) and their S and O in its tensor memory), tiles are 64
@@ -9,41 +9,44 @@
 //               CTA c supplies the rows of its 32 "own" tokens [32c, 32c+32)
 //   O += P V    M=128, N=256 dims (two MMAs), K=64 tokens; B is split by N:
 //               CTA c supplies latent tiles c and c+2 (its "PV half")
-// What changes is how rows reach shared memory.  A producer warp turns each
-// top-k entry into a slot and issues TMA tile::gather4 copies (four rows per
-// instruction) into a ring of raw fp8 stages; the dequant warps read those
-// stages from shared memory instead of issuing global loads of their own, so
-// the bytes in flight are bounded by the ring, not by L1, and no dequant warp
-// waits on a global load.  A raw stage holds half a tile for this CTA: 16 own
-// rows whole (656 B: latent, scales, rope) and the PV half of 16 rows of the
-// other CTA (tiles c and c+2, 128 B each, and the 16 B of scales), fetched
-// through three tensor maps over the pool (whole rows, 128-byte tiles,
-// scales).  A masked slot fetches row 0 and is flagged invalid: its K and V
-// rows are written as zeros and its score is replaced by -inf in the softmax
-// (validity bits per tile), so a fully masked row still gives P = 0 and
-// LSE = -inf.
+// Rows reach shared memory two ways.  A CTA's 32 own rows per tile (656 B
+// each, 21 KB) come whole by TMA: a producer warp turns top-k entries into
+// slots and issues 8 tile::gather4 copies (four rows each) into a 2-stage
+// raw ring, so those bytes bypass L1 and no warp waits for them.  The PV
+// half of the other CTA's 32 rows (272 B each) is loaded into registers by
+// the dequant warps that handle those rows, one tile ahead, issued right
+// after the step's proxy fence so that no fence waits on loads in flight.
+// A masked slot fetches row 0 (TMA) or nothing (registers) and is flagged
+// invalid: its K and V rows are zeros and its score is replaced by -inf in
+// the softmax (validity bits per tile), so a fully masked row still gives
+// P = 0 and LSE = -inf.
+//
+// K and V of a tile are signalled separately: QK(j) waits for the K rows
+// only, PV(j) for the V rows, so with two V stages the dequant of tile j
+// never waits for PV(j-2) before QK(j) can start.
 //
 // Tensor memory (512 columns, both CTAs), as decode_tc2.cu:
 //   [  0,256)  O, dims [0,256) MMA in [0,128), dims [256,512) MMA in [128,256)
 //   [256,320)  2 S buffers x 32 fp32 columns
 //   [320,512)  Q dims [0,384), the A operand of 24 k-steps (lanes L and L^64
 //              hold the same head)
-// Shared memory (about 225 KB):
+// Shared memory (about 219 KB):
 //   q    Q dims [384,576): 3 x 64-dim swizzled blocks of 64 rows      24 KB
 //   k    2 stages: own 32 tokens x 576 dims, 9 blocks of 32 rows      72 KB
 //   v    2 stages: 64 tokens x PV-half dims, 4 blocks of 64 rows      64 KB
 //   p    2 stages: P (bf16) of 64 heads x 64 tokens                   16 KB
-//   raw  3 half-tile stages of gathered fp8 rows                      45 KB
+//   raw  2 stages: the tile's 32 own rows as gathered by TMA          42 KB
 //
 // Warp roles (448 threads per CTA):
 //   warps 0-3   softmax + epilogue (thread L = TMEM lane L)
 //   warp 4      TMEM allocation in both CTAs; lane 0 of the even CTA issues
 //               every MMA of the pair
 //   warps 5-12  dequant: part A = the PV half of the 64 tile rows (V stage,
-//               and the K stage for own rows), part B = the other half and
-//               the rope of the 32 own rows (K stage)
+//               and the K stage for own rows; the other CTA's rows loaded
+//               into registers here), part B = the other half and the rope
+//               of the 32 own rows (K stage)
 //   warp 13     producer: indices -> slots (block table included for the
-//               paged entry point) -> gather4 into the raw ring
+//               paged entry point) -> gather4 of own rows into the raw ring
 // Barriers that gate the issuing thread live in the even CTA and count
 // arrivals of both CTAs; pair-MMA completion reaches both CTAs through a
 // multicast commit.  Every wait is bounded; after a failed wait a role stops,
@@ -81,15 +84,12 @@ constexpr int kVStageBytes = 4 * kVBlockBytes;
 constexpr int kVStages = 2;
 constexpr int kPStageBytes = 64 * 128;    // 64 heads x 64 tokens bf16
 constexpr int kPStages = 2;
-// raw ring: a stage is half a tile of this CTA's rows
-constexpr int kHalfRows = kOwn / 2;              // 16 own rows + 16 rows of the other CTA
-constexpr int kOwnGroupBytes = 2688;             // 4 whole rows (2624 B), 128-B multiple
-constexpr int kOthGroupBytes = 1152;             // 4 rows: tile c 512 | tile c+2 512 | scales 64 (+64)
-constexpr int kOthBase = 4 * kOwnGroupBytes;     // 10752
-constexpr int kRawStageBytes = kOthBase + 4 * kOthGroupBytes;  // 15360
-constexpr int kRawStages = 3;
-constexpr uint32_t kRawTx = kHalfRows * kRowBytes + kHalfRows * (2 * kTile + 16);  // 14848
-constexpr int kVMaskSlots = 4;
+// raw ring: a stage is one tile's 32 own rows, 8 gather4 groups of 4 rows
+constexpr int kGroupBytes = 2688;         // 4 whole rows (2624 B), 128-B multiple
+constexpr int kRawStageBytes = 8 * kGroupBytes;
+constexpr int kRawStages = 2;
+constexpr uint32_t kRawTx = kOwn * kRowBytes;  // 20992
+constexpr int kMaskSlots = 4;
 constexpr int kSoftmaxWarps = 4;
 constexpr int kMmaWarp = 4;
 constexpr int kFirstLoadWarp = 5;
@@ -112,14 +112,14 @@ struct Smem {
   uint8_t raw[kRawStages][kRawStageBytes];  // gather4 destinations (128-B aligned)
   float pmax[2][128];                       // partial tile max, by tile parity
   float lsum[128];                          // partial row sums (epilogue)
-  uint8_t rvalid[kRawStages][2 * kHalfRows];  // per raw row: own 0..15, other 16..31
-  uint32_t vmask[kVMaskSlots][2];           // tile rows [0,32) and [32,64) live bits
+  uint8_t rvalid[kRawStages][kOwn];         // own row live (producer's flags)
+  uint32_t vmask[kMaskSlots][2];            // tile rows [0,32) and [32,64) live bits
   uint64_t raw_full[kRawStages], raw_empty[kRawStages];
-  uint64_t tfull[kKStages];                 // even CTA: tile j's K and V in both CTAs
+  uint64_t kready[kKStages], vready[kVStages];  // even CTA: tile j's K / V rows in both CTAs
   uint64_t kempty[kKStages], vempty[kVStages];
   uint64_t sfull[2], pfull[kPStages], pempty[kPStages];
   uint64_t xch[2];
-  uint64_t vfull[kVMaskSlots];              // this CTA: tile's validity bits written
+  uint64_t mfull[kMaskSlots];               // this CTA: the tile's live bits written
   uint64_t qready, ofull, drain;
   uint32_t tmem_base;
 };
@@ -134,11 +134,6 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) {
   return r * 128u + ((c ^ (r & 7u)) << 4);
 }
 
-struct Rows {
-  uint4 a[4], asc;
-  uint4 b[2], brope, bsc;
-};
-
 struct Ctx {
   const DecodeArgs* a;
   const int32_t* idx_row;
@@ -147,9 +142,9 @@ struct Ctx {
   uint32_t rank;
   uint32_t tmem;
   uint32_t sq, sk0, sv0, sp0;
-  uint32_t b_tfull, b_kempty, b_vempty, b_sfull, b_pfull, b_pempty;
+  uint32_t b_kready, b_vready, b_kempty, b_vempty, b_sfull, b_pfull, b_pempty;
   uint32_t b_xch, b_qready, b_ofull, b_drain;
-  uint32_t b_rawfull, b_rawempty, b_vfull;
+  uint32_t b_rawfull, b_rawempty, b_mfull;
 };
 
 // ------------------------------------------------------------------ MMA issuer (even CTA)
@@ -177,8 +172,12 @@ __device__ void mma_role(const Ctx& c) {
   const uint64_t kdesc0 = sdesc_sw128(c.sk0, 16, 1024);
   const uint64_t pdesc0 = sdesc_sw128(c.sp0, 16, 1024);
   const uint64_t vdesc0 = sdesc_sw128(c.sv0, kVBlockBytes, 1024);
-  auto issue_pv = [&](int jj) {
+  // PV(jj): waits for P(jj) (softmax of both CTAs) and V(jj) (dequant of both)
+  auto issue_pv = [&](int jj) -> bool {
     const int ps = jj % kPStages, vs = jj % kVStages;
+    if (!thread_wait_cluster(c.b_pfull + 8 * ps, (jj / kPStages) & 1, 36)) return false;
+    if (!thread_wait_cluster(c.b_vready + 8 * vs, (jj / kVStages) & 1, 38)) return false;
+    tc_fence_after();
     const uint64_t pd = pdesc0 + (uint64_t)((ps * kPStageBytes) >> 4);
     const uint64_t vd = vdesc0 + (uint64_t)((vs * kVStageBytes) >> 4);
 #pragma unroll
@@ -190,32 +189,22 @@ __device__ void mma_role(const Ctx& c) {
                     (jj > 0 || kk > 0) ? 1u : 0u);
     mma_commit_pair(c.b_pempty + 8 * ps);
     mma_commit_pair(c.b_vempty + 8 * vs);
+    return true;
   };
   for (int j = 0; j < c.ntiles && ok; ++j) {
     const int b = j & 1, ks = j % kKStages;
-    ok = thread_wait_cluster(c.b_tfull + 8 * ks, (j / kKStages) & 1, 37);
+    ok = thread_wait_cluster(c.b_kready + 8 * ks, (j / kKStages) & 1, 37);
     if (!ok) break;
     tc_fence_after();
     issue_qk(c.tmem + kColS + kSBufCols * b, tQ, qdesc0,
              kdesc0 + (uint64_t)((ks * kKStageBytes) >> 4));
     mma_commit_pair(c.b_sfull + 8 * b);
     mma_commit_pair(c.b_kempty + 8 * ks);
-    if (j >= 1) {
-      const int jp = j - 1;
-      ok = thread_wait_cluster(c.b_pfull + 8 * (jp % kPStages), (jp / kPStages) & 1, 36);
-      if (!ok) break;
-      tc_fence_after();
-      issue_pv(jp);
-    }
+    if (j >= 1) ok = issue_pv(j - 1);
   }
   if (ok && c.ntiles > 0) {
-    const int jl = c.ntiles - 1;
-    ok = thread_wait_cluster(c.b_pfull + 8 * (jl % kPStages), (jl / kPStages) & 1, 36);
-    if (ok) {
-      tc_fence_after();
-      issue_pv(jl);
-      mma_commit_pair(c.b_ofull);
-    }
+    ok = issue_pv(c.ntiles - 1);
+    if (ok) mma_commit_pair(c.b_ofull);
   }
   // drain: nothing this thread issued may still touch either CTA's memory
   mma_commit_pair(c.b_drain);
@@ -223,25 +212,19 @@ __device__ void mma_role(const Ctx& c) {
 }
 
 // ------------------------------------------------------------------ producer
-// Half-stage hs (tile hs >> 1, half hs & 1) holds own rows [16h, 16h+16) of
-// this CTA's 32 and the other CTA's rows [16h, 16h+16) of its 32.  Lane i < 16
-// takes own row i, lane 16 + i the other CTA's row i.
+// Tile j's own rows: lane i takes own row i (tile row 32c + i); lanes 0-7 each
+// gather four of them.
 template <bool kPaged>
-__device__ void producer(const Ctx& c, Smem& s, const CUtensorMap* tm_row, const CUtensorMap* tm_tile,
-                         const CUtensorMap* tm_scale, int lane) {
+__device__ void producer(const Ctx& c, Smem& s, const CUtensorMap* tm, int lane) {
   const DecodeArgs& a = *c.a;
   const int cr = (int)c.rank;
-  const int nhs = 2 * c.ntiles;
-  // tile row of this lane's entry in half-stage hs
-  const int rsub = lane & 15;
-  const int rbase = lane < 16 ? kOwn * cr : kOwn * (1 - cr);
-  auto raw_at = [&](int hs) -> int32_t {
-    if (hs >= nhs) return -1;
-    const int pos = c.beg + (hs >> 1) * kN + rbase + 16 * (hs & 1) + rsub;
+  auto raw_at = [&](int j) -> int32_t {
+    if (j >= c.ntiles) return -1;
+    const int pos = c.beg + j * kN + kOwn * cr + lane;
     return pos < c.end ? c.idx_row[pos] : -1;
   };
-  // index pipeline: raw entries two half-stages ahead (flat), or three ahead
-  // with the block-table read two ahead (paged), so no step waits on a load
+  // index pipeline: raw entries two tiles ahead (flat), or three ahead with
+  // the block-table read two ahead (paged), so no step waits on a load
   int32_t r1 = raw_at(0), r2 = raw_at(1);
   SlotPf f1{-1, 0};
   if constexpr (kPaged) {
@@ -249,73 +232,57 @@ __device__ void producer(const Ctx& c, Smem& s, const CUtensorMap* tm_row, const
     r1 = r2;
     r2 = raw_at(2);
   }
-  // gather4 assignment: lanes 0-3 whole own rows (group g = lane), lanes 4-15
-  // the other CTA's rows (group g = (lane-4)/3; tile c, tile c+2, scales)
-  const int og = (lane - 4) / 3, kind = (lane - 4) % 3;
-  const int src = lane < 4 ? 4 * lane : 16 + 4 * og;
-  uint32_t dst_off = 0;
-  const CUtensorMap* tm = tm_row;
-  int32_t x = 0;
-  if (lane < 4) {
-    dst_off = lane * kOwnGroupBytes;
-  } else if (lane < 16) {
-    dst_off = kOthBase + og * kOthGroupBytes + kind * 512;
-    tm = kind < 2 ? tm_tile : tm_scale;
-    x = kind < 2 ? 16 * (cr + 2 * kind) : 64;
-  }
   bool ok = true;
   int armed = 0;
-  for (int hs = 0; hs < nhs; ++hs) {
+  for (int j = 0; j < c.ntiles; ++j) {
     int32_t slot;
     if constexpr (kPaged) {
       slot = slot_finish(a, f1);
       f1 = slot_fetch(a, c.req, r1);
       r1 = r2;
-      r2 = raw_at(hs + 3);
+      r2 = raw_at(j + 3);
     } else {
       slot = live_slot(a, c.req, r1);
       r1 = r2;
-      r2 = raw_at(hs + 2);
+      r2 = raw_at(j + 2);
     }
-    const int st = hs % kRawStages;
-    if (hs >= kRawStages)
-      ok = warp_wait(c.b_rawempty + 8 * st, ((hs / kRawStages) + 1) & 1, 40);
+    const int st = j % kRawStages;
+    if (j >= kRawStages) ok = warp_wait(c.b_rawempty + 8 * st, ((j / kRawStages) + 1) & 1, 40);
     if (!ok) break;
     s.rvalid[st][lane] = slot >= 0 ? 1 : 0;
     const int32_t row = slot >= 0 ? slot : 0;  // masked: a valid row, flagged invalid
-    const int32_t g0 = __shfl_sync(0xFFFFFFFFu, row, src & 31);
-    const int32_t g1 = __shfl_sync(0xFFFFFFFFu, row, (src + 1) & 31);
-    const int32_t g2 = __shfl_sync(0xFFFFFFFFu, row, (src + 2) & 31);
-    const int32_t g3 = __shfl_sync(0xFFFFFFFFu, row, (src + 3) & 31);
+    const int src = (4 * lane) & 31;
+    const int32_t g0 = __shfl_sync(0xFFFFFFFFu, row, src);
+    const int32_t g1 = __shfl_sync(0xFFFFFFFFu, row, src + 1);
+    const int32_t g2 = __shfl_sync(0xFFFFFFFFu, row, src + 2);
+    const int32_t g3 = __shfl_sync(0xFFFFFFFFu, row, src + 3);
     const uint32_t bar = c.b_rawfull + 8 * st;
     __syncwarp();  // the flags (generic stores) are released by the arrive below
     if (lane == 0) mbar_arrive_expect_tx(bar, kRawTx);
     __syncwarp();
-    if (lane < 16) tma_gather4(smem_u32(s.raw[st]) + dst_off, tm, x, g0, g1, g2, g3, bar);
+    if (lane < 8) tma_gather4(smem_u32(s.raw[st]) + lane * kGroupBytes, tm, 0, g0, g1, g2, g3, bar);
     ++armed;
   }
   // the stages armed last have landed before the producer returns, even
   // after a failed wait (full limit)
-  for (int xh = armed > kRawStages ? armed - kRawStages : 0; xh < armed; ++xh)
-    (void)warp_wait(c.b_rawfull + 8 * (xh % kRawStages), (xh / kRawStages) & 1, 41);
+  for (int x = armed > kRawStages ? armed - kRawStages : 0; x < armed; ++x)
+    (void)warp_wait(c.b_rawfull + 8 * (x % kRawStages), (x / kRawStages) & 1, 41);
 }
 
 // ------------------------------------------------------------------ dequant
+template <bool kPaged>
 __device__ void dequant_role(const Ctx& c, Smem& s, int lw, int lane) {
+  const DecodeArgs& a = *c.a;
   const int cr = (int)c.rank;
-  // part A: tile row rowA, lane quarter pA: PV-half chunks pA + 4i
+  // part A: tile row rowA, lane quarter pA: PV-half chunks pA + 4i.  A warp's
+  // eight part-A rows are all own rows or all rows of the other CTA.
   const int rowA = lw * 8 + (lane & 7), pA = lane >> 3;
   const bool ownA = (rowA >> 5) == cr;
-  const int oA = rowA & 31, hA = oA >> 4, iA = oA & 15;
+  const int oA = rowA & 31;
   // part B: own row rowB (own index), lane eighth qB
   const int rowB = lw * 4 + (lane >> 3), qB = lane & 7;
-  const int hB = rowB >> 4, iB = rowB & 15;
-  // byte offsets inside a raw stage
-  const uint32_t offA = ownA ? (uint32_t)((iA >> 2) * kOwnGroupBytes + (iA & 3) * kRowBytes)
-                             : (uint32_t)(kOthBase + (iA >> 2) * kOthGroupBytes + (iA & 3) * kTile);
-  const uint32_t offB = (uint32_t)((iB >> 2) * kOwnGroupBytes + (iB & 3) * kRowBytes);
-  const uint32_t offAsc = ownA ? offA + kScaleOff
-                               : (uint32_t)(kOthBase + (iA >> 2) * kOthGroupBytes + 1024 + (iA & 3) * 16);
+  const uint32_t offA = (uint32_t)((oA >> 2) * kGroupBytes + (oA & 3) * kRowBytes);
+  const uint32_t offB = (uint32_t)((rowB >> 2) * kGroupBytes + (rowB & 3) * kRowBytes);
   auto deq = [&](const uint4& w, float sc, uint4& o0, uint4& o1) {
     dequant4_hw_x2(w.x, sc, o0.x, o0.y);
     dequant4_hw_x2(w.y, sc, o0.z, o0.w);
@@ -326,91 +293,158 @@ __device__ void dequant_role(const Ctx& c, Smem& s, int lw, int lane) {
     return __uint_as_float(tile == 0 ? sc.x : tile == 1 ? sc.y : tile == 2 ? sc.z : sc.w);
   };
   const uint4 z4 = make_uint4(0, 0, 0, 0);
-  bool ok = true;
-  for (int j = 0; j < c.ntiles && ok; ++j) {
-    const int hs0 = 2 * j, hs1 = 2 * j + 1;
-    const int stA = (hs0 + hA) % kRawStages, stB = (hs0 + hB) % kRawStages;
-    ok = warp_wait(c.b_rawfull + 8 * (hs0 % kRawStages), (hs0 / kRawStages) & 1, 42);
-    if (ok) ok = warp_wait(c.b_rawfull + 8 * (hs1 % kRawStages), (hs1 / kRawStages) & 1, 42);
-    if (!ok) break;
-    // every lane acquires the two stages' copies itself before reading them
-    (void)mbar_try_wait(c.b_rawfull + 8 * (hs0 % kRawStages), (hs0 / kRawStages) & 1);
-    (void)mbar_try_wait(c.b_rawfull + 8 * (hs1 % kRawStages), (hs1 / kRawStages) & 1);
-    Rows R;
-    const uint8_t* ra = s.raw[stA];
-    const bool vA = s.rvalid[stA][(ownA ? 0 : 16) + iA] != 0;
-    const bool vB = s.rvalid[stB][iB] != 0;
-    if (vA) {
+
+  // ---- the other CTA's rows (warps with !ownA): slots and register loads
+  // one tile ahead.  Lane i < 8 converts the index of part-A row lw*8 + i; the
+  // slot reaches the lanes of that row by shuffle.
+  auto raw_at = [&](int j) -> int32_t {
+    if (ownA || lane >= 8 || j >= c.ntiles) return -1;
+    const int pos = c.beg + j * kN + lw * 8 + lane;
+    return pos < c.end ? c.idx_row[pos] : -1;
+  };
+  uint4 A[4], Asc;
+  bool vAnext = false;
+  auto load_other = [&](int32_t sl) {
+    const int32_t sa = __shfl_sync(0xFFFFFFFFu, sl, lane & 7);
+    vAnext = sa >= 0;
+    if (sa >= 0) {
+      const uint8_t* src = a.kv + sa * (int64_t)kRowBytes;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int tile = cr + 2 * (i >> 1);
-        const int chunk = pA + 4 * (i & 1);
-        // own rows: tile t at 128 t; other rows: tile c at 0, tile c+2 at 512
-        const uint32_t o = ownA ? offA + 128 * tile + 16 * chunk : offA + 512 * (i >> 1) + 16 * chunk;
-        R.a[i] = *reinterpret_cast<const uint4*>(ra + o);
+        A[i] = ldg_v4(src + 128 * tile + 16 * (pA + 4 * (i & 1)));
       }
-      R.asc = *reinterpret_cast<const uint4*>(ra + offAsc);
+      Asc = ldg_v4(src + kScaleOff);
     } else {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) R.a[i] = z4;
-      R.asc = z4;
+      for (int i = 0; i < 4; ++i) A[i] = z4;
+      Asc = z4;
     }
-    if (vB) {
-      const uint8_t* rb = s.raw[stB] + offB;
-      R.b[0] = *reinterpret_cast<const uint4*>(rb + 128 * (1 - cr) + 16 * qB);
-      R.b[1] = *reinterpret_cast<const uint4*>(rb + 128 * (3 - cr) + 16 * qB);
-      R.brope = *reinterpret_cast<const uint4*>(rb + kRopeOff + 16 * qB);
-      R.bsc = *reinterpret_cast<const uint4*>(rb + kScaleOff);
+  };
+  int32_t n1 = -1, n2 = -1;  // flat: raw entries of tiles j+1, j+2; paged: tiles j+2, j+3
+  SlotPf nf{-1, 0};           // paged: block-table read of tile j+1
+  if (!ownA) {
+    const int32_t s0 = live_slot(a, c.req, raw_at(0));
+    if (c.ntiles > 0) load_other(s0);
+    if constexpr (kPaged) {
+      nf = slot_fetch(a, c.req, raw_at(1));
+      n1 = raw_at(2);
+      n2 = raw_at(3);
     } else {
-      R.b[0] = R.b[1] = R.brope = R.bsc = z4;
+      n1 = raw_at(1);
+      n2 = raw_at(2);
+    }
+  }
+  bool ok = true;
+  for (int j = 0; j < c.ntiles && ok; ++j) {
+    const int st = j % kRawStages;
+    ok = warp_wait(c.b_rawfull + 8 * st, (j / kRawStages) & 1, 42);
+    if (!ok) break;
+    (void)mbar_try_wait(c.b_rawfull + 8 * st, (j / kRawStages) & 1);  // every lane acquires
+    const uint8_t* rs = s.raw[st];
+    bool vA;
+    if (ownA) {
+      vA = s.rvalid[st][oA] != 0;
+      if (vA) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int tile = cr + 2 * (i >> 1);
+          A[i] = *reinterpret_cast<const uint4*>(rs + offA + 128 * tile + 16 * (pA + 4 * (i & 1)));
+        }
+        Asc = *reinterpret_cast<const uint4*>(rs + offA + kScaleOff);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) A[i] = z4;
+        Asc = z4;
+      }
+    } else {
+      vA = vAnext;
+    }
+    const bool vB = s.rvalid[st][rowB] != 0;
+    uint4 B0 = z4, B1 = z4, Brope = z4, Bsc = z4;
+    if (vB) {
+      const uint8_t* rb = rs + offB;
+      B0 = *reinterpret_cast<const uint4*>(rb + 128 * (1 - cr) + 16 * qB);
+      B1 = *reinterpret_cast<const uint4*>(rb + 128 * (3 - cr) + 16 * qB);
+      Brope = *reinterpret_cast<const uint4*>(rb + kRopeOff + 16 * qB);
+      Bsc = *reinterpret_cast<const uint4*>(rb + kScaleOff);
     }
     // the tile's live bits: lanes 0-7 hold part-A rows [8 lw, 8 lw + 8)
     const uint32_t bits = __ballot_sync(0xFFFFFFFFu, vA) & 0xFFu;
+    // part A in bf16 (used for the own rows' K and for V)
+    uint4 Ab[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) deq(A[i], pick(Asc, cr + 2 * (i >> 1)), Ab[2 * i], Ab[2 * i + 1]);
     __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(c.b_rawempty + 8 * (hs0 % kRawStages));
-      mbar_arrive(c.b_rawempty + 8 * (hs1 % kRawStages));
-    }
+    if (lane == 0) mbar_arrive(c.b_rawempty + 8 * st);  // the raw stage is in registers
+
+    // ---- K rows: part A own rows, part B
     const int ks = j % kKStages, vs = j % kVStages;
     if (j >= kKStages) ok = warp_wait_cluster(c.b_kempty + 8 * ks, ((j / kKStages) + 1) & 1, 43);
-    if (ok && j >= kVStages) ok = warp_wait_cluster(c.b_vempty + 8 * vs, ((j / kVStages) + 1) & 1, 44);
     if (!ok) break;
     // live bits of tile j into slot j % 4: its previous reader, the softmax of
     // tile j - 4, handed over P(j - 4) before PV(j - 4) was issued, and that
     // precedes QK(j - 2), whose completion the K-stage wait above saw
-    if (lane == 0) reinterpret_cast<uint8_t*>(s.vmask[j % kVMaskSlots])[lw] = (uint8_t)bits;
+    if (lane == 0) reinterpret_cast<uint8_t*>(s.vmask[j % kMaskSlots])[lw] = (uint8_t)bits;
     uint8_t* kst = s.k[ks];
-    uint8_t* vst = s.v[vs];
+    if (ownA) {
+      const int r = rowA - kOwn * cr;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int tile = cr + 2 * (i >> 1);
-      uint4 o0, o1;
-      deq(R.a[i], pick(R.asc, tile), o0, o1);
-      uint8_t* vb = vst + i * kVBlockBytes;
-      *reinterpret_cast<uint4*>(vb + swz(rowA, 2 * pA)) = o0;
-      *reinterpret_cast<uint4*>(vb + swz(rowA, 2 * pA + 1)) = o1;
-      if (ownA) {
+      for (int i = 0; i < 4; ++i) {
+        const int tile = cr + 2 * (i >> 1);
         uint8_t* kb = kst + (2 * tile + (i & 1)) * kKBlockBytes;
-        const int r = rowA - kOwn * cr;
-        *reinterpret_cast<uint4*>(kb + swz(r, 2 * pA)) = o0;
-        *reinterpret_cast<uint4*>(kb + swz(r, 2 * pA + 1)) = o1;
+        *reinterpret_cast<uint4*>(kb + swz(r, 2 * pA)) = Ab[2 * i];
+        *reinterpret_cast<uint4*>(kb + swz(r, 2 * pA + 1)) = Ab[2 * i + 1];
       }
     }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int tile = (1 - cr) + 2 * i;
+    {
       uint4 o0, o1;
-      deq(R.b[i], pick(R.bsc, tile), o0, o1);
-      uint8_t* kb = kst + (2 * tile + (qB >> 2)) * kKBlockBytes;
+      deq(B0, pick(Bsc, 1 - cr), o0, o1);
+      uint8_t* kb = kst + (2 * (1 - cr) + (qB >> 2)) * kKBlockBytes;
+      *reinterpret_cast<uint4*>(kb + swz(rowB, 2 * (qB & 3))) = o0;
+      *reinterpret_cast<uint4*>(kb + swz(rowB, 2 * (qB & 3) + 1)) = o1;
+      deq(B1, pick(Bsc, 3 - cr), o0, o1);
+      kb = kst + (2 * (3 - cr) + (qB >> 2)) * kKBlockBytes;
       *reinterpret_cast<uint4*>(kb + swz(rowB, 2 * (qB & 3))) = o0;
       *reinterpret_cast<uint4*>(kb + swz(rowB, 2 * (qB & 3) + 1)) = o1;
     }
-    *reinterpret_cast<uint4*>(kst + 8 * kKBlockBytes + swz(rowB, qB)) = R.brope;
+    *reinterpret_cast<uint4*>(kst + 8 * kKBlockBytes + swz(rowB, qB)) = Brope;
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      mbar_arrive(c.b_vfull + 8 * (j % kVMaskSlots));  // this CTA's softmax: live bits
-      mbar_arrive_cluster(c.b_tfull + 8 * ks, 0);       // the issuing CTA: K and V rows
+      mbar_arrive(c.b_mfull + 8 * (j % kMaskSlots));  // this CTA's softmax: live bits
+      mbar_arrive_cluster(c.b_kready + 8 * ks, 0);    // the issuing CTA: K rows
+    }
+
+    // ---- V rows: part A, all 64 rows
+    if (j >= kVStages) ok = warp_wait_cluster(c.b_vempty + 8 * vs, ((j / kVStages) + 1) & 1, 44);
+    if (!ok) break;
+    uint8_t* vst = s.v[vs];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint8_t* vb = vst + i * kVBlockBytes;
+      *reinterpret_cast<uint4*>(vb + swz(rowA, 2 * pA)) = Ab[2 * i];
+      *reinterpret_cast<uint4*>(vb + swz(rowA, 2 * pA + 1)) = Ab[2 * i + 1];
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(c.b_vready + 8 * vs, 0);
+
+    // ---- the other CTA's rows of tile j+1: issued after the fences above,
+    // so no fence of this warp waits for them
+    if (!ownA && j + 1 < c.ntiles) {
+      int32_t s1;
+      if constexpr (kPaged) {
+        s1 = slot_finish(a, nf);
+        nf = slot_fetch(a, c.req, n1);
+        n1 = n2;
+        n2 = raw_at(j + 4);
+      } else {
+        s1 = live_slot(a, c.req, n1);
+        n1 = n2;
+        n2 = raw_at(j + 3);
+      }
+      load_other(s1);
     }
   }
 }
@@ -419,9 +453,7 @@ __device__ void dequant_role(const Ctx& c, Smem& s, int lw, int lane) {
 
 template <bool kPaged>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    decode_tc3_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_row,
-                      const __grid_constant__ CUtensorMap tm_tile,
-                      const __grid_constant__ CUtensorMap tm_scale) {
+    decode_tc3_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_row) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t pad = ((raw_base + 1023u) & ~1023u) - raw_base;
@@ -447,7 +479,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   c.sk0 = smem_u32(s.k[0]);
   c.sv0 = smem_u32(s.v[0]);
   c.sp0 = smem_u32(s.p[0]);
-  c.b_tfull = smem_u32(&s.tfull[0]);
+  c.b_kready = smem_u32(&s.kready[0]);
+  c.b_vready = smem_u32(&s.vready[0]);
   c.b_kempty = smem_u32(&s.kempty[0]);
   c.b_vempty = smem_u32(&s.vempty[0]);
   c.b_sfull = smem_u32(&s.sfull[0]);
@@ -459,7 +492,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   c.b_drain = smem_u32(&s.drain);
   c.b_rawfull = smem_u32(&s.raw_full[0]);
   c.b_rawempty = smem_u32(&s.raw_empty[0]);
-  c.b_vfull = smem_u32(&s.vfull[0]);
+  c.b_mfull = smem_u32(&s.mfull[0]);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRawStages; ++i) {
@@ -467,10 +500,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(c.b_rawempty + 8 * i, kLoadWarps);
     }
     for (int i = 0; i < kKStages; ++i) {
-      mbar_init(c.b_tfull + 8 * i, 2 * kLoadWarps);
+      mbar_init(c.b_kready + 8 * i, 2 * kLoadWarps);
       mbar_init(c.b_kempty + 8 * i, 1);
     }
-    for (int i = 0; i < kVStages; ++i) mbar_init(c.b_vempty + 8 * i, 1);
+    for (int i = 0; i < kVStages; ++i) {
+      mbar_init(c.b_vready + 8 * i, 2 * kLoadWarps);
+      mbar_init(c.b_vempty + 8 * i, 1);
+    }
     for (int i = 0; i < 2; ++i) {
       mbar_init(c.b_sfull + 8 * i, 1);
       mbar_init(c.b_xch + 8 * i, kSoftmaxWarps);
@@ -479,7 +515,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(c.b_pfull + 8 * i, 2 * kSoftmaxWarps);
       mbar_init(c.b_pempty + 8 * i, 1);
     }
-    for (int i = 0; i < kVMaskSlots; ++i) mbar_init(c.b_vfull + 8 * i, kLoadWarps);
+    for (int i = 0; i < kMaskSlots; ++i) mbar_init(c.b_mfull + 8 * i, kLoadWarps);
     mbar_init(c.b_qready, 2 * kSoftmaxWarps);
     mbar_init(c.b_ofull, 1);
     mbar_init(c.b_drain, 1);
@@ -554,10 +590,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int j = 0; j < c.ntiles && ok; ++j) {
       const int b = j & 1, ps = j % kPStages;
       ok = warp_wait_cluster(c.b_sfull + 8 * b, (j >> 1) & 1, 31);
-      if (ok) ok = warp_wait(c.b_vfull + 8 * (j % kVMaskSlots), (j / kVMaskSlots) & 1, 30);
+      if (ok) ok = warp_wait(c.b_mfull + 8 * (j % kMaskSlots), (j / kMaskSlots) & 1, 30);
       if (!ok) break;
-      (void)mbar_try_wait(c.b_vfull + 8 * (j % kVMaskSlots), (j / kVMaskSlots) & 1);
-      const uint32_t live = s.vmask[j % kVMaskSlots][hh];  // tokens [32 hh, 32 hh + 32)
+      (void)mbar_try_wait(c.b_mfull + 8 * (j % kMaskSlots), (j / kMaskSlots) & 1);
+      const uint32_t live = s.vmask[j % kMaskSlots][hh];  // tokens [32 hh, 32 hh + 32)
       tc_fence_after();
       uint32_t sv[32];
       tmem_ld32(trow + kColS + kSBufCols * b, sv);
@@ -673,9 +709,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (rank == 0 && lane == 0) mma_role(c);
     __syncwarp();
   } else if (warp == kProducerWarp) {
-    producer<kPaged>(c, s, &tm_row, &tm_tile, &tm_scale, lane);
+    producer<kPaged>(c, s, &tm_row, lane);
   } else {
-    dequant_role(c, s, warp - kFirstLoadWarp, lane);
+    dequant_role<kPaged>(c, s, warp - kFirstLoadWarp, lane);
   }
 
   // both CTAs: no MMA of the pair may still run, no arrival may still target
@@ -711,16 +747,15 @@ int read_device_status_tc3(unsigned int* status, bool reset, cudaStream_t st) {
 }
 
 int launch_decode_tc3(const DecodeArgs& a, cudaStream_t st) {
-  CUtensorMap maps[3];
-  if (int rc = encode_row_map(&maps[0], a.kv, a.num_slots, kRowBytes / 8)) return rc;
-  if (int rc = encode_row_map(&maps[1], a.kv, a.num_slots, kTile / 8)) return rc;
-  if (int rc = encode_row_map(&maps[2], a.kv, a.num_slots, 2)) return rc;
+  // the pool as [num_slots] rows of 82 uint64: one gather4 box = 4 whole rows
+  CUtensorMap map;
+  if (int rc = encode_row_map(&map, a.kv, a.num_slots, kRowBytes / 8)) return rc;
   const size_t smem = sizeof(tc3::Smem) + 1024;  // + alignment slack
   auto go = [&](auto kern) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return check_cuda(e, "decode_tc3 smem attribute");
     dim3 grid((unsigned)(a.T * a.G * 2), a.num_splits);
-    return check_cuda(launch_pdl(kern, grid, dim3(tc3::kThreads), smem, st, a, maps[0], maps[1], maps[2]),
+    return check_cuda(launch_pdl(kern, grid, dim3(tc3::kThreads), smem, st, a, map),
                       "decode_tc3_kernel launch");
   };
   const int rc = a.block_table != nullptr ? go(tc3::decode_tc3_kernel<true>)
