@@ -118,7 +118,7 @@ FP8MLA_API int64_t fp8mla_decode_workspace_bytes(int64_t T, int64_t H, int64_t G
 
 /*
  * Name of the decode kernel fp8mla_sparse_decode dispatches for this shape
- * ("decode_tc2_kernel" for 128 or 64 heads per kv group with bf16 q,
+ * ("decode_tc3_kernel" for 128 or 64 heads per kv group with bf16 q,
  * "decode_ws_kernel" for other head counts with bf16 q and a non-empty pool,
  * "decode_mma_kernel" for fp32 q; "+merge_splits_kernel" is appended when the
  * call splits the top-k axis; the name string stays valid until the calling
@@ -142,7 +142,9 @@ FP8MLA_API const char* fp8mla_decode_kernel_name(int64_t T, int64_t H, int64_t G
  *                          unit stride on the last dim.
  *   kv       [num_slots, 656] uint8, contiguous, 16-byte aligned.
  *   indices  [T, G, topk]  int32 flat slot indices; entries < 0 or
- *                          >= num_slots are masked (no load is issued).
+ *                          >= num_slots are masked: they contribute nothing
+ *                          and no address is formed from them (the TMA-staged
+ *                          kernels fetch row 0 in their place and discard it).
  *                          Head h reads group h / (H / G).
  *   sm_scale softmax scale WITHOUT the log2(e) factor.
  *   out      [T, H, 512]   same dtype as q.

@@ -21,8 +21,8 @@ CSRC = os.path.join(HERE, "csrc")
 OUT_DIR = os.path.join(HERE, "vllm_fp8kv")
 LIB = os.path.join(OUT_DIR, "libfp8mla.so")
 OBJ_DIR = os.path.join(HERE, "_build")
-SOURCES = ["abi.cu", "abi_noalloc.cu", "unit_kernels.cu", "decode_mma.cu", "decode_tc2.cu",
-           "decode_tc3.cu", "decode_ws.cu"]
+SOURCES = ["abi.cu", "abi_noalloc.cu", "unit_kernels.cu", "decode_mma.cu", "decode_tc3.cu",
+           "decode_ws.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -4,8 +4,6 @@
 // kernel dispatch, and the thread-local error message.
 #include <stdarg.h>
 #include <stdio.h>
-#include <stdlib.h>
-#include <string.h>
 
 #include <atomic>
 #include <mutex>
@@ -111,17 +109,6 @@ int64_t ws_bytes(int64_t T, int64_t H, int S, int elem_bytes) {
 }
 }  // namespace
 
-// The TMA-staged pair kernel serves every pair shape whose pool its tensor
-// maps can address; FP8MLA_PAIR_KERNEL=tc2 selects the register-gather one
-// (for side-by-side measurements).
-bool use_tc3(const DecodeArgs& a) {
-  static const bool force_tc2 = [] {
-    const char* e = getenv("FP8MLA_PAIR_KERNEL");
-    return e != nullptr && strcmp(e, "tc2") == 0;
-  }();
-  return !force_tc2 && decode_tc3_supported(a);
-}
-
 int device_sm_count() {
   const DevInfo* d = dev_info();
   return (d && d->sms > 0) ? d->sms : 148;
@@ -143,11 +130,10 @@ int fp8mla_device_status(unsigned int* status, int reset, void* stream) {
   *status = 0;
   if (int rc = require_sm100()) return rc;
   // each kernel file keeps its own status word
-  unsigned int v1 = 0, v2 = 0, v3 = 0;
-  int rc = read_device_status(&v1, reset != 0, static_cast<cudaStream_t>(stream));
-  if (rc == FP8MLA_OK) rc = read_device_status_ws(&v2, reset != 0, static_cast<cudaStream_t>(stream));
+  unsigned int v2 = 0, v3 = 0;
+  int rc = read_device_status_ws(&v2, reset != 0, static_cast<cudaStream_t>(stream));
   if (rc == FP8MLA_OK) rc = read_device_status_tc3(&v3, reset != 0, static_cast<cudaStream_t>(stream));
-  *status = v1 | v2 | v3;
+  *status = v2 | v3;
   return rc;
 }
 
@@ -205,10 +191,9 @@ const char* fp8mla_decode_kernel_name(int64_t T, int64_t H, int64_t G, int64_t t
   a.block_h = a.hpg < 16 ? a.hpg : 16;
   a.num_slots = 1;  // names the kernel of a non-empty pool
   a.num_splits = S < 1 ? 1 : S;
-  const char* k = !decode_tc_supported(a)  ? (decode_ws_supported(a) ? "decode_ws_kernel"
-                                                                     : "decode_mma_kernel")
-                  : use_tc3(a)              ? "decode_tc3_kernel"
-                                            : "decode_tc2_kernel";
+  const char* k = decode_tc3_supported(a)  ? "decode_tc3_kernel"
+                  : decode_ws_supported(a) ? "decode_ws_kernel"
+                                           : "decode_mma_kernel";
   if (a.num_splits == 1) return k;
   static thread_local char buf[64];
   snprintf(buf, sizeof(buf), "%s+merge_splits_kernel", k);
@@ -311,7 +296,7 @@ int decode_impl(const void* q, int q_dtype, int64_t T, int64_t H, int64_t q_stri
       if ((int64_t)1 << k == paged->block_size) a.block_shift = k;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (decode_tc_supported(a)) return use_tc3(a) ? launch_decode_tc3(a, st) : launch_decode_tc2(a, st);
+  if (decode_tc3_supported(a)) return launch_decode_tc3(a, st);
   if (decode_ws_supported(a)) return launch_decode_ws(a, device_sm_count(), st);
   return launch_decode_mma(a, st);
 }

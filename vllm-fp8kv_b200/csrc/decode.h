@@ -124,10 +124,7 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream
 
 int launch_decode_mma(const DecodeArgs& a, cudaStream_t st);
 int launch_merge_splits(const DecodeArgs& a, cudaStream_t st);
-int read_device_status(unsigned int* status, bool reset, cudaStream_t st);
 int launch_wait_timeout_selftest(uint32_t iters, uint64_t* elapsed_ns, cudaStream_t st);
-bool decode_tc_supported(const DecodeArgs& a);
-int launch_decode_tc2(const DecodeArgs& a, cudaStream_t st);
 bool decode_tc3_supported(const DecodeArgs& a);
 int launch_decode_tc3(const DecodeArgs& a, cudaStream_t st);
 int read_device_status_tc3(unsigned int* status, bool reset, cudaStream_t st);

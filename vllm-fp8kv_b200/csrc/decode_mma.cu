@@ -1,6 +1,6 @@
 // decode_mma.cu -- split-KV sparse MLA decode over fp8_ds_mla pages for any
 // head count (the general path; 128 heads per kv group with bf16 q use the
-// paired tcgen05 kernel of decode_tc2.cu), plus the LSE merge of the split
+// paired tcgen05 kernel of decode_tc3.cu), plus the LSE merge of the split
 // partials.
 //
 // One CTA = (query token, block of <= 16 heads, split of the top-k axis).

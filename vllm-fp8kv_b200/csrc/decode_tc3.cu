@@ -2,13 +2,24 @@
 // pair of SMs (a 2-CTA cluster) sharing cta_group::2 tcgen05 MMAs, with each
 // CTA's own rows staged in shared memory by TMA.
 //
-// The MMA side is decode_tc2.cu's: the pair splits the heads (CTA c owns
-// heads [64c, 64c+64) and their S and O in its tensor memory), tiles are 64
-// tokens, and
-//   S = Q K^T   M=128 heads, N=64 tokens, K=576 (36 k-steps); B is split by N:
-//               CTA c supplies the rows of its 32 "own" tokens [32c, 32c+32)
-//   O += P V    M=128, N=256 dims (two MMAs), K=64 tokens; B is split by N:
-//               CTA c supplies latent tiles c and c+2 (its "PV half")
+// The pair splits the heads, not the output dims: CTA c owns heads
+// [64c, 64c+64) and its TMEM holds their S and O.  A tile is 64 tokens and one
+// MMA spans both SMs:
+//   S = Q K^T   M=128 heads (64 per CTA), N=64 tokens, K=576 (36 k-steps); B
+//               is split by N: CTA c supplies the rows of its 32 "own" tokens
+//               [32c, 32c+32) of the tile, all 576 dims
+//   O += P V    M=128 heads, N=256 dims (two MMAs for the 512), K=64 tokens; B
+//               is split by N: CTA c supplies dims [128c, 128c+128) of each
+//               MMA, i.e. latent tiles c and c+2 (its "PV half"), all 64 tokens
+// So each CTA needs per tile its 32 own rows whole (656 B) and the PV half of
+// the other 32 rows (2 x 128 fp8 bytes + scales): the pair reads 59 KB of rows
+// per tile instead of 84 KB for two CTAs that each gather the whole tile.
+// Accumulator layout of an M=128 cta_group::2 MMA (measured): per CTA, lanes
+// [0,64) hold the CTA's 64 rows x columns [0, N/2), lanes [64,128) the same
+// rows x columns [N/2, N).  So softmax thread L (TMEM lane L) owns head
+// (L & 63) and tokens [32 (L >> 6), +32) of a tile; the two threads of a head
+// exchange their partial max through shared memory once per tile.
+//
 // Rows reach shared memory two ways.  A CTA's 32 own rows per tile (656 B
 // each, 21 KB) come whole by TMA: a producer warp turns top-k entries into
 // slots and issues 8 tile::gather4 copies (four rows each) into a 2-stage
@@ -25,28 +36,31 @@
 // only, PV(j) for the V rows, so with two V stages the dequant of tile j
 // never waits for PV(j-2) before QK(j) can start.
 //
-// Tensor memory (512 columns, both CTAs), as decode_tc2.cu:
+// Tensor memory (512 columns, both CTAs):
 //   [  0,256)  O, dims [0,256) MMA in [0,128), dims [256,512) MMA in [128,256)
 //   [256,320)  2 S buffers x 32 fp32 columns
 //   [320,512)  Q dims [0,384), the A operand of 24 k-steps (lanes L and L^64
 //              hold the same head)
-// Shared memory (about 219 KB):
+// Shared memory (about 221 KB):
 //   q    Q dims [384,576): 3 x 64-dim swizzled blocks of 64 rows      24 KB
 //   k    2 stages: own 32 tokens x 576 dims, 9 blocks of 32 rows      72 KB
 //   v    2 stages: 64 tokens x PV-half dims, 4 blocks of 64 rows      64 KB
 //   p    2 stages: P (bf16) of 64 heads x 64 tokens                   16 KB
 //   raw  2 stages: the tile's 32 own rows as gathered by TMA          42 KB
 //
-// Warp roles (448 threads per CTA):
+// Warp roles (480 threads per CTA; warp w runs on SM sub-partition w % 4):
 //   warps 0-3   softmax + epilogue (thread L = TMEM lane L)
 //   warp 4      TMEM allocation in both CTAs; lane 0 of the even CTA issues
 //               every MMA of the pair
-//   warps 5-12  dequant: part A = the PV half of the 64 tile rows (V stage,
+//   warp 8      producer: indices -> slots (block table included for the
+//               paged entry point) -> gather4 of own rows into the raw ring
+//   warps 5-7, 9-11, 13-14
+//               dequant: part A = the PV half of the 64 tile rows (V stage,
 //               and the K stage for own rows; the other CTA's rows loaded
 //               into registers here), part B = the other half and the rope
 //               of the 32 own rows (K stage)
-//   warp 13     producer: indices -> slots (block table included for the
-//               paged entry point) -> gather4 of own rows into the raw ring
+//   warp 12     idle (it keeps sub-partition 0, which issues the MMAs, free
+//               of dequant work: 88.0 vs 89.1 us per call at c2)
 // Barriers that gate the issuing thread live in the even CTA and count
 // arrivals of both CTAs; pair-MMA completion reaches both CTAs through a
 // multicast commit.  Every wait is bounded; after a failed wait a role stops,
@@ -92,10 +106,12 @@ constexpr uint32_t kRawTx = kOwn * kRowBytes;  // 20992
 constexpr int kMaskSlots = 4;
 constexpr int kSoftmaxWarps = 4;
 constexpr int kMmaWarp = 4;
-constexpr int kFirstLoadWarp = 5;
 constexpr int kLoadWarps = 8;
-constexpr int kProducerWarp = kFirstLoadWarp + kLoadWarps;  // 13
-constexpr int kThreads = (kProducerWarp + 1) * 32;          // 448
+constexpr int kProducerWarp = 8;
+constexpr int kIdleWarp = 12;
+constexpr int kThreads = 15 * 32;  // 480
+// dequant index of warp w (5-7, 9-11, 13-14 -> 0-7)
+__device__ __forceinline__ int dequant_index(int w) { return w < 8 ? w - 5 : w < 12 ? w - 6 : w - 7; }
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0, kColS = 256, kColQ = 320;
 constexpr uint32_t kSBufCols = kN / 2;  // 32
@@ -710,8 +726,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == kProducerWarp) {
     producer<kPaged>(c, s, &tm_row, lane);
-  } else {
-    dequant_role<kPaged>(c, s, warp - kFirstLoadWarp, lane);
+  } else if (warp != kIdleWarp) {
+    dequant_role<kPaged>(c, s, dequant_index(warp), lane);
   }
 
   // both CTAs: no MMA of the pair may still run, no arrival may still target
@@ -729,6 +745,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 bool decode_tc3_supported(const DecodeArgs& a) {
   return a.q_dtype == FP8MLA_DTYPE_BF16 && (a.hpg == tc3::kHeads || a.hpg == tc3::kHeads / 2) &&
          a.G >= 1 && a.num_slots > 0 && a.num_slots < (1ll << 31);
+}
+
+namespace {
+// Self-test of the bounded-wait error path: one warp runs the decode kernels'
+// wait loop (warp_wait_n) on an mbarrier that nothing arrives on.  It gives
+// up after `iters` try_wait calls, records the timeout (bits 8.. =
+// kSelftestWhere) in this file's status word and the kernel returns: no
+// fault, the context stays usable.
+constexpr unsigned int kSelftestWhere = 63;
+__device__ unsigned long long g_selftest_ns = 0;
+__global__ void __launch_bounds__(32) wait_timeout_selftest_kernel(uint32_t iters) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(smem_u32(&bar), 1);
+    tc::mbar_init_fence();
+  }
+  __syncwarp();
+  unsigned long long t0, t1;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  (void)tc::warp_wait_n(smem_u32(&bar), 0, kSelftestWhere, iters);
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+  if (threadIdx.x == 0) g_selftest_ns = t1 - t0;
+}
+}  // namespace
+
+int launch_wait_timeout_selftest(uint32_t iters, uint64_t* elapsed_ns, cudaStream_t st) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, st>>>(iters);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  unsigned long long ns = 0;
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&ns, g_selftest_ns, sizeof(ns));
+  if (elapsed_ns != nullptr) *elapsed_ns = ns;
+  return check_cuda(e, "wait timeout self-test");
 }
 
 int read_device_status_tc3(unsigned int* status, bool reset, cudaStream_t st) {

@@ -1,6 +1,6 @@
 // decode_ws.cu -- sparse MLA decode over fp8_ds_mla pages for bf16 q in head
 // blocks of <= 16 heads (small head counts; 64 or 128 heads per kv group take
-// the paired tcgen05 kernel of decode_tc2.cu, fp32 q the kernel of
+// the paired tcgen05 kernel of decode_tc3.cu, fp32 q the kernel of
 // decode_mma.cu): persistent, warp-specialised, rows gathered by TMA.
 //
 // One CTA per SM walks units u = blockIdx.x, blockIdx.x + gridDim.x, ...; a

@@ -5,9 +5,10 @@ Drop-in for the reference entry point of the same name
 asserts, same outputs.  The work runs in libfp8mla.so, which picks the
 kernel by head count and q dtype (``decode_kernel_name`` reports the choice):
 
-* 64 or 128 heads per kv group, bf16 q: ``decode_tc2_kernel``, a 2-SM cluster
+* 64 or 128 heads per kv group, bf16 q: ``decode_tc3_kernel``, a 2-SM cluster
   whose cta_group::2 tcgen05 MMAs take the heads as the M dimension (QK^T over
-  d=576 and PV over d_v=512, accumulators in tensor memory);
+  d=576 and PV over d_v=512, accumulators in tensor memory), rows staged by
+  TMA gather4;
 * any other head count with bf16 q: ``decode_ws_kernel``, persistent and
   warp-specialised, rows staged by TMA gather4;
 * fp32 q (the reference's CPU-test dtype): ``decode_mma_kernel``.
