@@ -233,3 +233,118 @@ def cosine(a, b) -> float:
     na = max(np.linalg.norm(a), 1e-8)
     nb = max(np.linalg.norm(b), 1e-8)
     return float(a @ b / (na * nb))
+
+
+# --------------------------------------------------------------- DSA indexer
+# The indexer of the sparse-MLA models scores every context token for each
+# query token and keeps the top-k positions that the decode then reads.  Its
+# key cache is a paged fp8 format of its own: per page of `block_size` tokens,
+# block_size x 128 e4m3 bytes followed by block_size fp32 scales (structure of
+# arrays; 8448 B at block_size 64, reference PORT_PLAN.md:14 and its trap 3).
+# The reference repository ships no code for this path; these restatements
+# follow vLLM 0.22's torch restatement of DeepGEMM's test reference
+# (installed vllm/v1/attention/ops/rocm_aiter_mla_sparse.py:256-354,
+# ``fp8_paged_mqa_logits_torch``, and :572-600, ``_topk_indices_torch``),
+# against which tests/golden/indexer.npz pins them.
+IDX_DIM = 128
+
+
+def indexer_page_bytes(block_size: int) -> int:
+    return block_size * (IDX_DIM + 4)
+
+
+def indexer_limit(context_len: int, next_n: int, n: int) -> int:
+    """Positions [0, limit) that query token n of next_n may score: the draft
+    tokens of a request sit at the end of its context, so token n sees up to
+    position context_len - next_n + n."""
+    return int(context_len) - next_n + n + 1
+
+
+def indexer_logits(q_u8: np.ndarray, kv_pages: np.ndarray, weights: np.ndarray,
+                   context_lens: np.ndarray, block_table: np.ndarray,
+                   max_model_len: int) -> np.ndarray:
+    """fp8 paged MQA logits.
+
+    q_u8      [B, next_n, H, 128] e4m3 bytes
+    kv_pages  [num_blocks, block_size * 132] uint8 pages (SoA as above)
+    weights   [B * next_n, H] fp32 (the query scale folded in by the caller)
+    -> logits [B * next_n, max_model_len] fp32:
+       sum_h relu(q[b, n, h] . k_s) * weights[b*next_n + n, h] * scale_s for
+       s < indexer_limit(context_len_b, next_n, n), -inf elsewhere.
+    Accumulated in fp64 (the reference's fp32 sums differ by rounding only).
+    """
+    q_u8 = np.asarray(q_u8, np.uint8)
+    B, nn, H, D = q_u8.shape
+    assert D == IDX_DIM
+    pages = np.asarray(kv_pages, np.uint8).reshape(kv_pages.shape[0], -1)
+    bs = pages.shape[1] // (D + 4)
+    q = e4m3_to_f32(q_u8).astype(np.float64).reshape(B, nn * H, D)
+    w = np.asarray(weights, np.float64).reshape(B, nn, H)
+    out = np.full((B * nn, max_model_len), -np.inf, np.float32)
+    for b in range(B):
+        ctx = int(context_lens[b])
+        if ctx <= 0:
+            continue
+        npg = -(-ctx // bs)
+        pg = pages[np.asarray(block_table[b, :npg], np.int64)]
+        k = e4m3_to_f32(pg[:, : bs * D]).astype(np.float64).reshape(npg * bs, D)
+        scale = np.ascontiguousarray(pg[:, bs * D:]).view(np.float32).reshape(npg * bs)
+        s = np.maximum(k @ q[b].T, 0.0).reshape(npg * bs, nn, H)
+        lg = (s * w[b][None]).sum(-1) * scale.astype(np.float64)[:, None]
+        for n in range(nn):
+            lim = min(indexer_limit(ctx, nn, n), max_model_len)
+            if lim > 0:
+                out[b * nn + n, :lim] = lg[:lim, n].astype(np.float32)
+    return out
+
+
+def _sortable_keys(v: np.ndarray) -> np.ndarray:
+    """fp32 -> uint32 keys whose unsigned order is the float order (NaN with
+    the sign bit clear sorts above +inf, as torch.topk ranks NaN highest)."""
+    u = np.ascontiguousarray(v, np.float32).view(np.uint32)
+    return np.where(u & 0x80000000, ~u, u | 0x80000000).astype(np.uint32)
+
+
+def indexer_topk(logits: np.ndarray, next_n: int, context_lens: np.ndarray,
+                 topk: int) -> np.ndarray:
+    """Top-k positions per logits row -> [rows, topk] int32.
+
+    Row r = b * next_n + n keeps positions [0, limit) (indexer_limit).  With
+    limit <= topk every position is kept; otherwise the topk largest logits,
+    ties at the threshold broken by the lower position.  The kept positions are
+    written in ascending order, then -1 (the decode's masked entry) pads the
+    row.  The set equals torch.topk's on untied values; the order is not part
+    of the contract (the decode treats indices as a set).
+    """
+    logits = np.asarray(logits, np.float32)
+    rows, L = logits.shape
+    out = np.full((rows, topk), -1, np.int32)
+    for r in range(rows):
+        b, n = divmod(r, next_n)
+        lim = min(L, indexer_limit(int(context_lens[b]), next_n, n))
+        if lim <= 0:
+            continue
+        if lim <= topk:
+            out[r, :lim] = np.arange(lim, dtype=np.int32)
+            continue
+        key = _sortable_keys(logits[r, :lim]).astype(np.int64)
+        order = np.lexsort((np.arange(lim), -key))
+        out[r] = np.sort(order[:topk]).astype(np.int32)
+    return out
+
+
+def indexer_quantize(k_f32: np.ndarray, block_size: int = 64) -> np.ndarray:
+    """Pack [N, 128] fp32 keys into SoA pages: per token scale = amax / 448
+    (1 for an all-zero row), bytes = e4m3(k / scale).  Test data only: the
+    indexer's own cache writer is not part of this library."""
+    k = np.asarray(k_f32, np.float32)
+    N, D = k.shape
+    assert D == IDX_DIM and N % block_size == 0
+    amax = np.abs(k).max(axis=1)
+    scale = np.where(amax > 0, amax / np.float32(448.0), np.float32(1.0)).astype(np.float32)
+    q8 = f32_to_e4m3((k / scale[:, None]).astype(np.float32))
+    nb = N // block_size
+    pages = np.empty((nb, block_size * (D + 4)), np.uint8)
+    pages[:, : block_size * D] = q8.reshape(nb, block_size * D)
+    pages[:, block_size * D:] = scale.reshape(nb, block_size).view(np.uint8).reshape(nb, block_size * 4)
+    return pages
