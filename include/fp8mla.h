@@ -284,6 +284,58 @@ FP8MLA_API int fp8mla_convert_req_index(const int32_t* req_id, const int32_t* bl
                              int64_t T, int64_t topk, int64_t block_size,
                              int32_t* out, int64_t out_stride, void* stream);
 
+/*
+ * DSA indexer read path, fp8 paged MQA logits.  Replaces the logits step the
+ * indexer runs before every sparse-MLA decode (reference specification:
+ * PORT_PLAN.md:14 and :41, D3; the reference ships no code for it;
+ * semantics of vLLM's `fp8_paged_mqa_logits`, whose torch restatement
+ * vllm/v1/attention/ops/rocm_aiter_mla_sparse.py:256-354 the tests pin to):
+ *
+ *   logits[b*next_n + n, s] = scale_s * sum_h relu(q[b,n,h] . k_s) * weights[b*next_n + n, h]
+ *
+ * for s < context_lens[b] - next_n + n + 1, and -inf for the other positions
+ * of the row up to max_model_len.
+ *
+ *   q            [B, next_n, H, head_dim] e4m3 bytes; a request's rows are
+ *                contiguous, requests q_stride_b bytes apart (16-byte aligned).
+ *   k_cache      [num_blocks, block_size * (head_dim + 4)] bytes: per block,
+ *                block_size x head_dim e4m3 values, then block_size fp32
+ *                scales (structure of arrays, 8448 bytes at block_size 64).
+ *   weights      [B * next_n, H] fp32 (row stride w_stride), the query scale
+ *                folded in.
+ *   context_lens [B] int32; block_table [B, bt_stride] int32 block ids
+ *                (positions past a valid block, or an id outside
+ *                [0, num_blocks), score -inf).
+ *   logits       [B * next_n, logits_stride] fp32, columns [0, max_model_len)
+ *                written.
+ * Supported: H = 64, head_dim = 128, block_size = 64, next_n = 1 or 2.
+ */
+FP8MLA_API int fp8mla_indexer_paged_logits(const uint8_t* q, int64_t B, int64_t next_n, int64_t H,
+                                           int64_t head_dim, int64_t q_stride_b,
+                                           const uint8_t* k_cache, int64_t num_blocks,
+                                           int64_t block_size, const float* weights,
+                                           int64_t w_stride, const int32_t* context_lens,
+                                           const int32_t* block_table, int64_t bt_stride,
+                                           int64_t max_blocks, float* logits,
+                                           int64_t logits_stride, int64_t max_model_len,
+                                           void* stream);
+
+/*
+ * Top-k positions of each indexer logits row: the step that fills the
+ * decode's top-k position buffer (`topk_indices_buffer`, read at the
+ * reference's backend_patch.py:79-81; vLLM's `top_k_per_row_decode`).  Row
+ * r = b * next_n + n keeps positions [0, limit) with limit =
+ * min(max_model_len, context_lens[b] - next_n + n + 1): all of them when
+ * limit <= topk, else the topk largest logits (ties at the threshold broken
+ * by the lower position).  Kept positions are written in ascending order,
+ * then -1 pads the row: out [rows, out_stride] int32, topk columns written.
+ * The set equals torch.topk's on untied values; the decode treats it as a set.
+ */
+FP8MLA_API int fp8mla_indexer_topk(const float* logits, int64_t rows, int64_t logits_stride,
+                                   int64_t next_n, const int32_t* context_lens, int32_t* out,
+                                   int64_t out_stride, int64_t topk, int64_t max_model_len,
+                                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

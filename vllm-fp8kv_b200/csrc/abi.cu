@@ -130,10 +130,11 @@ int fp8mla_device_status(unsigned int* status, int reset, void* stream) {
   *status = 0;
   if (int rc = require_sm100()) return rc;
   // each kernel file keeps its own status word
-  unsigned int v2 = 0, v3 = 0;
+  unsigned int v2 = 0, v3 = 0, v4 = 0;
   int rc = read_device_status_ws(&v2, reset != 0, static_cast<cudaStream_t>(stream));
   if (rc == FP8MLA_OK) rc = read_device_status_tc3(&v3, reset != 0, static_cast<cudaStream_t>(stream));
-  *status = v2 | v3;
+  if (rc == FP8MLA_OK) rc = read_device_status_idx(&v4, reset != 0, static_cast<cudaStream_t>(stream));
+  *status = v2 | v3 | v4;
   return rc;
 }
 
@@ -397,6 +398,52 @@ int fp8mla_convert_req_index(const int32_t* req_id, const int32_t* block_table,
   return launch_convert_req_index(req_id, block_table, bt_stride, max_blocks, token_idx,
                                   ti_stride, T, topk, block_size, out, out_stride,
                                   static_cast<cudaStream_t>(stream));
+}
+
+int fp8mla_indexer_paged_logits(const uint8_t* q, int64_t B, int64_t next_n, int64_t H,
+                                int64_t head_dim, int64_t q_stride_b, const uint8_t* k_cache,
+                                int64_t num_blocks, int64_t block_size, const float* weights,
+                                int64_t w_stride, const int32_t* context_lens,
+                                const int32_t* block_table, int64_t bt_stride, int64_t max_blocks,
+                                float* logits, int64_t logits_stride, int64_t max_model_len,
+                                void* stream) {
+  g_last_error[0] = 0;
+  if (H != 64 || head_dim != 128 || block_size != 64)
+    return set_error(FP8MLA_ERR_INVALID_ARGUMENT,
+                     "indexer logits take 64 heads of dim 128 over 64-token blocks (got H=%lld, "
+                     "dim=%lld, block_size=%lld)", (long long)H, (long long)head_dim,
+                     (long long)block_size);
+  if (next_n < 1 || next_n > 2)
+    return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "next_n must be 1 or 2, got %lld", (long long)next_n);
+  if (B < 0 || max_model_len < 0 || num_blocks < 0 || num_blocks >= (1LL << 31) || max_blocks < 0 ||
+      bt_stride < max_blocks || logits_stride < max_model_len || w_stride < H ||
+      q_stride_b < next_n * H * head_dim)
+    return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "bad indexer logits sizes or strides");
+  if (B == 0 || max_model_len == 0) return FP8MLA_OK;
+  if (num_blocks == 0)
+    return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "the indexer key cache is empty");
+  if (!aligned16(q) || q_stride_b % 16 != 0 || !aligned16(k_cache))
+    return set_error(FP8MLA_ERR_INVALID_ARGUMENT,
+                     "q and the key cache must be 16-byte aligned (q rows 16-byte strided)");
+  if (int rc = require_sm100()) return rc;
+  return launch_indexer_logits(q, B, next_n, q_stride_b, k_cache, num_blocks, weights, w_stride,
+                               context_lens, block_table, bt_stride, max_blocks, logits,
+                               logits_stride, max_model_len, device_sm_count(),
+                               static_cast<cudaStream_t>(stream));
+}
+
+int fp8mla_indexer_topk(const float* logits, int64_t rows, int64_t logits_stride, int64_t next_n,
+                        const int32_t* context_lens, int32_t* out, int64_t out_stride,
+                        int64_t topk, int64_t max_model_len, void* stream) {
+  g_last_error[0] = 0;
+  if (rows < 0 || next_n < 1 || rows % next_n != 0 || topk < 1 || topk > (1 << 20) ||
+      out_stride < topk || max_model_len < 0 || logits_stride < max_model_len ||
+      rows > (int64_t)INT32_MAX)
+    return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "bad indexer top-k sizes or strides");
+  if (rows == 0) return FP8MLA_OK;
+  if (int rc = require_sm100()) return rc;
+  return launch_indexer_topk(logits, rows, logits_stride, next_n, context_lens, out, out_stride, topk,
+                             max_model_len, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

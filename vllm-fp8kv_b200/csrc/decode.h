@@ -132,6 +132,16 @@ bool decode_ws_supported(const DecodeArgs& a);
 int launch_decode_ws(const DecodeArgs& a, int sms, cudaStream_t st);
 int read_device_status_ws(unsigned int* status, bool reset, cudaStream_t st);
 
+int read_device_status_idx(unsigned int* status, bool reset, cudaStream_t st);
+int launch_indexer_logits(const uint8_t* q, int64_t B, int64_t next_n, int64_t q_stride_b,
+                          const uint8_t* k_cache, int64_t num_blocks, const float* w,
+                          int64_t w_stride, const int32_t* ctx, const int32_t* bt, int64_t bt_stride,
+                          int64_t max_blocks, float* logits, int64_t logits_stride,
+                          int64_t max_len, int sms, cudaStream_t st);
+int launch_indexer_topk(const float* logits, int64_t rows, int64_t logits_stride, int64_t next_n,
+                        const int32_t* ctx, int32_t* out, int64_t out_stride, int64_t topk,
+                        int64_t max_len, cudaStream_t st);
+
 int launch_dequant(const uint8_t* in, int64_t n, void* out, int out_dtype, int method,
                    cudaStream_t st);
 int launch_dequant_rows(const uint8_t* kv, int64_t num_slots, const int32_t* slots, int64_t n,

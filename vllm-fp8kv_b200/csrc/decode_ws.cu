@@ -495,38 +495,6 @@ bool decode_ws_supported(const DecodeArgs& a) {
          a.block_h <= ws::kBH && a.T > 0;
 }
 
-namespace {
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
-                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
-                                   CUtensorMapFloatOOBfill);
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      p = nullptr;
-    return reinterpret_cast<EncodeTiledFn>(p);
-  }();
-  return fn;
-}
-}  // namespace
-
-int encode_row_map(CUtensorMap* tm, const uint8_t* kv, int64_t num_slots, uint32_t box_u64) {
-  EncodeTiledFn enc = encode_fn();
-  if (enc == nullptr) return set_error(FP8MLA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  const cuuint64_t dims[2] = {kRowBytes / 8, (cuuint64_t)num_slots};
-  const cuuint64_t strides[1] = {kRowBytes};
-  const cuuint32_t box[2] = {box_u64, 1};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(kv), dims, strides,
-                         box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(FP8MLA_ERR_CUDA, "tensor map encode failed (%d)", (int)r);
-  return FP8MLA_OK;
-}
-
 int launch_decode_ws(const DecodeArgs& a, int sms, cudaStream_t st) {
   // the pool as [num_slots] rows of 82 uint64: one gather4 box = 4 whole rows
   CUtensorMap tm;

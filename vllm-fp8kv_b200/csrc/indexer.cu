@@ -1,0 +1,519 @@
+// indexer.cu -- the read path of the sparse-MLA models' token indexer on
+// sm_100a: fp8 paged MQA logits (tcgen05, kind::f8f6f4) and the per-row top-k
+// that fills the decode's top-k position buffer.
+//
+// Key cache (vLLM's indexer cache, structure of arrays per block): a block of
+// 64 tokens is 64 x 128 e4m3 bytes followed by 64 fp32 scales, 8448 bytes
+// (reference PORT_PLAN.md:14 and trap 3).  Queries are e4m3 too, [B, next_n,
+// 64 heads, 128]; their scale is folded into `weights` by the caller.
+//
+//   logits[b*next_n + n, s] = scale_s * sum_h relu(q[b,n,h] . k_s) * w[b*next_n + n, h]
+//   for s < context_len_b - next_n + n + 1, and -inf elsewhere
+//
+// (vLLM 0.22's restatement of DeepGEMM's reference,
+// vllm/v1/attention/ops/rocm_aiter_mla_sparse.py:256-354, which the oracle and
+// the golden vectors follow.)  The reference repository has no code for this
+// path, only its specification.
+//
+// Logits kernel: one CTA handles a chunk of one request's context in tiles of
+// 128 tokens (two blocks).  The products are one MMA per 32 dims with the
+// tokens as M (128) and the request's next_n x 64 query heads as N:
+// D[token][head] = k_token . q_head, exact e4m3 x e4m3 products accumulated in
+// fp32, so that each epilogue thread (TMEM lane = token) reduces its own row
+// over the heads without talking to other threads.
+//   warps 0-3  epilogue: relu, weights, sum, scale, mask, store (coalesced)
+//   warp 4     producer: block ids from the block table, TMA copies of each
+//              block's values (one 3-D box, 128-byte swizzled) and a bulk copy
+//              of its 64 scales into a 5-stage ring
+//   warp 5     tensor memory allocation; lane 0 issues the MMAs
+// Two accumulator buffers in tensor memory let the epilogue of tile t overlap
+// the MMAs of tile t+1.  Every wait is bounded (status word, as the decode).
+//
+// Top-k kernel: one CTA per logits row.  Logits map to order-preserving
+// 32-bit keys; three histogram passes (11, 11 and 10 bits) find the k-th
+// largest key exactly; a final pass in position order writes every position
+// above it and the lowest-positioned ties, ascending, then -1 padding.
+#include "common.cuh"
+#include "decode.h"
+#include "tc_ptx.cuh"
+#include "tma_map.h"
+
+namespace fp8mla {
+namespace idx {
+
+using namespace fp8mla::tc;
+
+namespace {
+
+constexpr int kDim = 128;                 // index head dim (bytes per fp8 key row)
+constexpr int kHeads = 64;                // index heads per query token
+constexpr int kBlock = 64;                // tokens per cache block
+constexpr int kPageBytes = kBlock * (kDim + 4);   // 8448
+constexpr int kTileTokens = 128;          // MMA M: two blocks
+constexpr int kStages = 5;
+constexpr int kStageBytes = kTileTokens * kDim;   // 16 KB of values
+constexpr int kMaxNextN = 2;              // N = 64 * next_n query heads <= 128
+constexpr int kThreads = 6 * 32;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+
+// kind::f8f6f4 instruction descriptor: fp32 accumulate, A and B e4m3 (format
+// code 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+struct Smem {
+  uint8_t kv[kStages][kStageBytes];        // 1024-aligned: swizzled operand tiles
+  uint8_t q[kMaxNextN * kHeads * kDim];    // 1024-aligned: N rows of 128 B, swizzled
+  float scale[kStages][kTileTokens];
+  float w[kMaxNextN * kHeads];
+  uint8_t pvalid[kStages][2];              // block p of the stage's tile was loaded
+  uint64_t full[kStages], empty[kStages];
+  uint64_t tfull[2], tempty[2];
+  uint64_t qready, drain;
+  uint32_t tmem_base;
+};
+static_assert(offsetof(Smem, q) % 1024 == 0, "swizzle atoms need 1024-B alignment");
+static_assert(offsetof(Smem, full) % 8 == 0, "");
+
+struct Args {
+  const uint8_t* q;          // [B, next_n, 64, 128] e4m3, contiguous per request
+  int64_t q_stride_b;        // bytes between requests
+  const uint8_t* k_cache;    // [num_blocks, 8448]
+  int64_t num_blocks;
+  const float* w;            // [B * next_n, 64], row stride w_stride
+  int64_t w_stride;
+  const int32_t* ctx;        // [B]
+  const int32_t* bt;         // [B, bt_stride]
+  int64_t bt_stride, max_blocks;
+  float* logits;             // [B * next_n, logits_stride]
+  int64_t logits_stride, max_len;
+  int next_n;
+  int tiles_per_cta;
+};
+
+// The epilogue warps' own barrier (id 1; the other warps never use it).
+__device__ __forceinline__ void named_sync_epi() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t swz128(uint32_t r, uint32_t c) {  // row r, 16-B chunk c
+  return r * 128u + ((c ^ (r & 7u)) << 4);
+}
+
+__device__ __forceinline__ void mma_f8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_page(uint32_t dst, const CUtensorMap* tm, int32_t block,
+                                              uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(dst),
+      "l"(tm), "r"(0), "r"(0), "r"(block), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+}  // namespace
+
+namespace {
+
+// ------------------------------------------------------------------ logits
+__device__ void producer(const Args& a, Smem& s, const CUtensorMap* tm, int b, int t0, int ncomp,
+                         int ctx) {
+  int armed = 0;
+  bool ok = true;
+  for (int i = 0; i < ncomp; ++i) {
+    const int st = i % kStages, t = t0 + i;
+    if (i >= kStages) ok = thread_wait(smem_u32(&s.empty[st]), ((i / kStages) + 1) & 1, 50);
+    if (!ok) break;
+    int32_t bid[2];
+    uint32_t bytes = 0;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int64_t pos = 2 * (int64_t)t + p;  // block of the request
+      bid[p] = -1;
+      if ((int64_t)t * kTileTokens + p * kBlock < ctx && pos < a.max_blocks) {
+        const int32_t v = a.bt[(int64_t)b * a.bt_stride + pos];
+        if (v >= 0 && v < a.num_blocks) bid[p] = v;
+      }
+      s.pvalid[st][p] = bid[p] >= 0 ? 1 : 0;
+      if (bid[p] >= 0) bytes += kBlock * kDim + kBlock * 4;
+    }
+    const uint32_t bar = smem_u32(&s.full[st]);
+    mbar_arrive_expect_tx(bar, bytes);  // releases the flags above
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      if (bid[p] < 0) continue;
+      tma_load_page(smem_u32(s.kv[st]) + p * kBlock * kDim, tm, bid[p], bar);
+      bulk_g2s(smem_u32(&s.scale[st][p * kBlock]),
+               a.k_cache + (int64_t)bid[p] * kPageBytes + kBlock * kDim, kBlock * 4, bar);
+    }
+    ++armed;
+  }
+  // no copy may outlive the CTA: the stages armed last have landed (full limit)
+  for (int x = armed > kStages ? armed - kStages : 0; x < armed; ++x)
+    (void)thread_wait(smem_u32(&s.full[x % kStages]), (x / kStages) & 1, 51);
+}
+
+__device__ void mma_issuer(const Args& a, Smem& s, uint32_t tmem, int ncomp, int N) {
+  bool ok = thread_wait(smem_u32(&s.qready), 0, 52);
+  tc_fence_after();
+  const uint64_t qdesc = sdesc_sw128(smem_u32(s.q), 16, 1024);
+  const uint32_t idesc = idesc_e4m3(kTileTokens, N);
+  for (int i = 0; i < ncomp && ok; ++i) {
+    const int st = i % kStages, buf = i & 1;
+    ok = thread_wait(smem_u32(&s.full[st]), (i / kStages) & 1, 53);
+    if (ok && i >= 2) ok = thread_wait(smem_u32(&s.tempty[buf]), ((i >> 1) + 1) & 1, 54);
+    if (!ok) break;
+    tc_fence_after();
+    const uint64_t adesc = sdesc_sw128(smem_u32(s.kv[st]), 16, 1024);
+#pragma unroll
+    for (int k = 0; k < kDim / 32; ++k)  // 32 e4m3 values = 32 bytes per k-step
+      mma_f8(tmem + buf * N, adesc + (uint64_t)((k * 32) >> 4), qdesc + (uint64_t)((k * 32) >> 4),
+             idesc, k > 0 ? 1u : 0u);
+    mma_commit(smem_u32(&s.empty[st]));
+    mma_commit(smem_u32(&s.tfull[buf]));
+  }
+  // drain: no MMA may still run when tensor memory is freed
+  mma_commit(smem_u32(&s.drain));
+  (void)thread_wait(smem_u32(&s.drain), 0, 55);
+}
+
+__device__ void epilogue(const Args& a, Smem& s, uint32_t tmem, int b, int t0, int ntiles,
+                         int ncomp, int ctx, int N) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = threadIdx.x;  // TMEM lane = token of the tile
+  const int nn = a.next_n;
+  // the request's query rows (swizzled K-major operand) and head weights
+  const uint4* qsrc = reinterpret_cast<const uint4*>(a.q + (int64_t)b * a.q_stride_b);
+  for (int c = threadIdx.x; c < N * (kDim / 16); c += 128) {
+    const int row = c >> 3, chunk = c & 7;
+    *reinterpret_cast<uint4*>(s.q + swz128(row, chunk)) = qsrc[c];
+  }
+  for (int c = threadIdx.x; c < N; c += 128)
+    s.w[c] = a.w[((int64_t)b * nn + c / kHeads) * a.w_stride + (c % kHeads)];
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(smem_u32(&s.qready));
+  named_sync_epi();  // s.w is read by every epilogue thread below
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  bool ok = true;
+  for (int i = 0; i < ntiles; ++i) {
+    const int64_t tok = (int64_t)(t0 + i) * kTileTokens + r;
+    float v[kMaxNextN];
+#pragma unroll
+    for (int n = 0; n < kMaxNextN; ++n) v[n] = -INFINITY;
+    if (i < ncomp && ok) {
+      const int st = i % kStages, buf = i & 1;
+      ok = warp_wait(smem_u32(&s.tfull[buf]), (i >> 1) & 1, 56);
+      if (ok) ok = warp_wait(smem_u32(&s.full[st]), (i / kStages) & 1, 57);
+      if (ok) {
+        (void)mbar_try_wait(smem_u32(&s.full[st]), (i / kStages) & 1);  // every lane acquires
+        tc_fence_after();
+        float acc[kMaxNextN];
+#pragma unroll
+        for (int n = 0; n < kMaxNextN; ++n) {
+          acc[n] = 0.f;
+          if (n < nn) {
+            uint32_t d0[32], d1[32];
+            tmem_ld32(trow + buf * N + n * kHeads, d0);
+            tmem_ld32(trow + buf * N + n * kHeads + 32, d1);
+            tmem_wait_ld();
+            const float* w = s.w + n * kHeads;
+#pragma unroll
+            for (int h = 0; h < 32; ++h) {
+              acc[n] = fmaf(fmaxf(__uint_as_float(d0[h]), 0.f), w[h], acc[n]);
+              acc[n] = fmaf(fmaxf(__uint_as_float(d1[h]), 0.f), w[32 + h], acc[n]);
+            }
+          }
+        }
+        const float sc = s.scale[st][r];
+        const bool live = s.pvalid[st][r >> 6] != 0;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(smem_u32(&s.tempty[buf]));  // accumulator buffer read
+          mbar_arrive(smem_u32(&s.empty[st]));    // scales and flags read
+        }
+#pragma unroll
+        for (int n = 0; n < kMaxNextN; ++n)
+          if (n < nn && live && tok < (int64_t)ctx - nn + n + 1) v[n] = acc[n] * sc;
+      }
+    }
+    if (tok < a.max_len) {
+#pragma unroll
+      for (int n = 0; n < kMaxNextN; ++n)
+        if (n < nn) a.logits[((int64_t)b * nn + n) * a.logits_stride + tok] = v[n];
+    }
+  }
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1)
+    indexer_logits_kernel(const Args a, const __grid_constant__ CUtensorMap tm) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t pad = ((raw_base + 1023u) & ~1023u) - raw_base;
+  Smem& s = *reinterpret_cast<Smem*>(smem_raw + pad);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y;
+  const int N = kHeads * a.next_n;
+  const uint32_t tmem_cols = N <= 64 ? 128u : 256u;  // two accumulator buffers
+  const int total_tiles = (int)((a.max_len + kTileTokens - 1) / kTileTokens);
+  const int t0 = blockIdx.x * a.tiles_per_cta;
+  const int ntiles = max(0, min(a.tiles_per_cta, total_tiles - t0));
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(smem_u32(&s.full[i]), 1);
+      mbar_init(smem_u32(&s.empty[i]), 1 + 4);  // the MMAs' commit + the 4 epilogue warps
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&s.tfull[i]), 1);
+      mbar_init(smem_u32(&s.tempty[i]), 4);
+    }
+    mbar_init(smem_u32(&s.qready), 4);
+    mbar_init(smem_u32(&s.drain), 1);
+    mbar_init_fence();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32(&s.tmem_base), tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  pdl_wait();  // the previous kernel of the stream has completed: global memory from here on
+  const uint32_t tmem = s.tmem_base;
+  const int ctx = max(0, a.ctx[b]);
+  // tiles with a token below the context are computed; the rest are -inf
+  const int ctx_tiles = (int)(((int64_t)ctx + kTileTokens - 1) / kTileTokens);
+  const int ncomp = max(0, min(ntiles, ctx_tiles - t0));
+
+  if (warp < 4) {
+    epilogue(a, s, tmem, b, t0, ntiles, ncomp, ctx, N);
+  } else if (warp == kProducerWarp) {
+    if (lane == 0) producer(a, s, &tm, b, t0, ncomp, ctx);
+    __syncwarp();
+  } else {
+    if (lane == 0) mma_issuer(a, s, tmem, ncomp, N);
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, tmem_cols);
+  }
+}
+
+// ------------------------------------------------------------------ top-k
+constexpr int kTopkThreads = 1024;
+
+__device__ __forceinline__ uint32_t sortable_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Block-wide exclusive scan of v over 1024 threads; returns this thread's
+// prefix and writes the total to *total (every thread).
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* warp_sums, uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = warp_sums[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, w, o);
+      if (lane >= o) w += y;
+    }
+    warp_sums[lane] = w;  // inclusive over warps
+  }
+  __syncthreads();
+  const uint32_t before = (warp > 0 ? warp_sums[warp - 1] : 0u) + (x - v);
+  *total = warp_sums[31];
+  __syncthreads();  // warp_sums is reused by the next call
+  return before;
+}
+
+__global__ void __launch_bounds__(kTopkThreads)
+    indexer_topk_kernel(const float* logits, int64_t logits_stride, int next_n, const int32_t* ctx,
+                        int32_t* out, int64_t out_stride, int k, int64_t max_len) {
+  __shared__ uint32_t hist[2048];
+  __shared__ uint32_t warp_sums[32];
+  __shared__ uint32_t sel[2];  // chosen bin, keys above it (this pass)
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  pdl_wait();
+  const int64_t r = blockIdx.x;
+  const int b = (int)(r / next_n), n = (int)(r % next_n);
+  const int64_t lim = min(max_len, (int64_t)ctx[b] - next_n + n + 1);
+  const float* row = logits + r * logits_stride;
+  int32_t* o = out + r * out_stride;
+  if (lim <= k) {  // every position kept, then padding
+    for (int i = threadIdx.x; i < k; i += kTopkThreads) o[i] = i < lim ? i : -1;
+    return;
+  }
+  // radix select of the k-th largest key: 11 + 11 + 10 bits
+  uint32_t prefix = 0, pmask = 0, remaining = (uint32_t)k;
+#pragma unroll 1
+  for (int pass = 0; pass < 3; ++pass) {
+    const int shift = pass == 0 ? 21 : pass == 1 ? 10 : 0;
+    const int nbins = pass == 2 ? 1024 : 2048;
+    for (int i = threadIdx.x; i < nbins; i += kTopkThreads) hist[i] = 0;
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < lim; i += kTopkThreads) {
+      const uint32_t key = sortable_key(row[i]);
+      if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & (nbins - 1)], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      // lane l owns bins [nbins - per*(l+1), nbins - per*l), scanned from the top
+      const int lane = threadIdx.x, per = nbins / 32;
+      const int hi = nbins - per * lane;
+      uint32_t sum = 0;
+      for (int bi = hi - 1; bi >= hi - per; --bi) sum += hist[bi];
+      uint32_t incl = sum;
+#pragma unroll
+      for (int o2 = 1; o2 < 32; o2 <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o2);
+        if (lane >= o2) incl += y;
+      }
+      const uint32_t excl = incl - sum;
+      const bool mine = excl < remaining && incl >= remaining;
+      if (mine) {
+        uint32_t above = excl;
+        int bi = hi - 1;
+        for (; bi > hi - per; --bi) {
+          if (above + hist[bi] >= remaining) break;
+          above += hist[bi];
+        }
+        sel[0] = (uint32_t)bi;
+        sel[1] = above;
+      }
+    }
+    __syncthreads();
+    prefix |= sel[0] << shift;
+    pmask |= (uint32_t)(nbins - 1) << shift;
+    remaining -= sel[1];
+    __syncthreads();  // sel and hist are rewritten by the next pass
+  }
+  // prefix is the k-th largest key; `remaining` of the keys equal to it are
+  // kept (the lowest positions), every key above it too
+  uint32_t base_g = 0, base_e = 0;
+  constexpr int kItems = 4;
+  for (int64_t start = 0; start < lim; start += (int64_t)kTopkThreads * kItems) {
+    const int64_t i0 = start + (int64_t)threadIdx.x * kItems;
+    uint32_t keys[kItems];
+    uint32_t cg = 0, ce = 0;
+#pragma unroll
+    for (int j = 0; j < kItems; ++j) {
+      keys[j] = (i0 + j < lim) ? sortable_key(row[i0 + j]) : 0u;
+      const bool valid = i0 + j < lim;
+      cg += (valid && keys[j] > prefix) ? 1u : 0u;
+      ce += (valid && keys[j] == prefix) ? 1u : 0u;
+    }
+    uint32_t tot;
+    const uint32_t ex = block_excl_scan((cg << 16) | ce, warp_sums, &tot);
+    uint32_t g = base_g + (ex >> 16), e = base_e + (ex & 0xFFFFu);
+#pragma unroll
+    for (int j = 0; j < kItems; ++j) {
+      if (i0 + j >= lim) break;
+      if (keys[j] > prefix) {
+        o[g + min(e, remaining)] = (int32_t)(i0 + j);
+        ++g;
+      } else if (keys[j] == prefix) {
+        if (e < remaining) o[g + e] = (int32_t)(i0 + j);
+        ++e;
+      }
+    }
+    base_g += tot >> 16;
+    base_e += tot & 0xFFFFu;
+  }
+}
+
+}  // namespace idx
+
+// ------------------------------------------------------------------ host
+int read_device_status_idx(unsigned int* status, bool reset, cudaStream_t st) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, tc::g_device_status, sizeof(v), 0,
+                                            cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && reset && v != 0) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbolAsync(tc::g_device_status, &zero, sizeof(zero), 0,
+                                cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  }
+  *status = v;
+  return check_cuda(e, "device status read");
+}
+
+int launch_indexer_logits(const uint8_t* q, int64_t B, int64_t next_n, int64_t q_stride_b,
+                          const uint8_t* k_cache, int64_t num_blocks, const float* w,
+                          int64_t w_stride, const int32_t* ctx, const int32_t* bt, int64_t bt_stride,
+                          int64_t max_blocks, float* logits, int64_t logits_stride,
+                          int64_t max_len, int sms, cudaStream_t st) {
+  CUtensorMap tm;
+  if (int rc = encode_indexer_page_map(&tm, k_cache, num_blocks, idx::kBlock, idx::kDim)) return rc;
+  idx::Args a{};
+  a.q = q;
+  a.q_stride_b = q_stride_b;
+  a.k_cache = k_cache;
+  a.num_blocks = num_blocks;
+  a.w = w;
+  a.w_stride = w_stride;
+  a.ctx = ctx;
+  a.bt = bt;
+  a.bt_stride = bt_stride;
+  a.max_blocks = max_blocks;
+  a.logits = logits;
+  a.logits_stride = logits_stride;
+  a.max_len = max_len;
+  a.next_n = (int)next_n;
+  // chunks of up to 16 tiles (2048 tokens); smaller chunks when the batch would
+  // leave SMs idle (two CTAs fit an SM)
+  const int64_t total_tiles = (max_len + idx::kTileTokens - 1) / idx::kTileTokens;
+  int64_t tpc = 16;
+  while (tpc > 2 && B * ((total_tiles + tpc - 1) / tpc) < 2 * (int64_t)sms) tpc >>= 1;
+  a.tiles_per_cta = (int)tpc;
+  const size_t smem = sizeof(idx::Smem) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(idx::indexer_logits_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return check_cuda(e, "indexer logits smem attribute");
+  const dim3 grid((unsigned)((total_tiles + tpc - 1) / tpc), (unsigned)B);
+  return check_cuda(launch_pdl(idx::indexer_logits_kernel, grid, dim3(idx::kThreads), smem, st, a, tm),
+                    "indexer_logits_kernel launch");
+}
+
+int launch_indexer_topk(const float* logits, int64_t rows, int64_t logits_stride, int64_t next_n,
+                        const int32_t* ctx, int32_t* out, int64_t out_stride, int64_t topk,
+                        int64_t max_len, cudaStream_t st) {
+  return check_cuda(launch_pdl(idx::indexer_topk_kernel, dim3((unsigned)rows), dim3(idx::kTopkThreads),
+                               0, st, logits, logits_stride, (int)next_n, ctx, out, out_stride,
+                               (int)topk, max_len),
+                    "indexer_topk_kernel launch");
+}
+
+}  // namespace fp8mla

@@ -57,6 +57,13 @@ SIGNATURES = {
     "fp8mla_ds_mla_dequant_rows": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I32, _P]),
     "fp8mla_convert_req_index": (_I32, [_P, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64,
                                         _P, _I64, _P]),
+    "fp8mla_indexer_paged_logits": (_I32, [
+        _P, _I64, _I64, _I64, _I64, _I64,      # q, B, next_n, H, head_dim, q_stride_b
+        _P, _I64, _I64,                        # k_cache, num_blocks, block_size
+        _P, _I64,                              # weights, w_stride
+        _P, _P, _I64, _I64,                    # context_lens, block_table, bt_stride, max_blocks
+        _P, _I64, _I64, _P]),                  # logits, logits_stride, max_model_len, stream
+    "fp8mla_indexer_topk": (_I32, [_P, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _P]),
 }
 
 _lib = None
