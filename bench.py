@@ -450,13 +450,98 @@ def run_ours(args, rank, world, local_rank):
     return line
 
 
+# ---------------------------------------------------------------- indexer
+def run_indexer(args):
+    """The DSA indexer read path at the headline's request shape: 64 decode
+    tokens (next_n 1), 64 index heads of dim 128, 32768-token contexts over
+    their own fp8 key pages (random page permutations), top-2048 selection.
+    One step = fp8_paged_mqa_logits + top_k_per_row_decode over one batch;
+    four rotating query sets, keys 277 MB > L2."""
+    import torch
+
+    from vllm_fp8kv.indexer import PAGE_BYTES, fp8_paged_mqa_logits, indexer_topk
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, ctx, topk, nb_per = 64, 32768, 2048, 32768 // 64
+    g = torch.Generator(device=dev).manual_seed(7)
+    nb = B * nb_per
+    k = torch.randn((nb * 64, 128), generator=g, device=dev)
+    scale = (k.abs().amax(1) / 448.0).clamp_min(1e-30)
+    kq = (k / scale[:, None]).to(torch.float8_e4m3fn).view(torch.uint8).view(nb, 64 * 128)
+    pages = torch.empty((nb, PAGE_BYTES), dtype=torch.uint8, device=dev)
+    pages[:, : 64 * 128] = kq
+    pages[:, 64 * 128:] = scale.view(nb, 64).contiguous().view(torch.uint8)
+    del k, kq
+    bt = torch.randperm(nb, generator=g, device=dev).view(B, nb_per).to(torch.int32)
+    ctxs = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+    sets = []
+    for _ in range(N_SETS):
+        q = torch.randn((B, 1, 64, 128), generator=g, device=dev).to(torch.float8_e4m3fn)
+        w = torch.randn((B, 64), generator=g, device=dev) / 8
+        sets.append((q, w))
+    logits = torch.empty((B, ctx), dtype=torch.float32, device=dev)
+    out = torch.empty((B, topk), dtype=torch.int32, device=dev)
+
+    def step(i, what="both"):
+        q, w = sets[i % N_SETS]
+        if what in ("both", "logits"):
+            fp8_paged_mqa_logits(q, pages, w, ctxs, bt, None, ctx, logits=logits)
+        if what in ("both", "topk"):
+            from vllm_fp8kv.indexer import top_k_per_row_decode
+
+            top_k_per_row_decode(logits, 1, ctxs, out, B, logits.stride(0), 1, topk)
+
+    stream = torch.cuda.current_stream(dev)
+    clk = ClockSampler(0)
+    clk.__enter__()
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    times = {}
+    for what in ("both", "logits", "topk"):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i, what)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        times[what] = e0.elapsed_time(e1) / args.steps
+    clk.__exit__(None, None, None)
+    key_bytes = B * ctx * 132
+    logit_bytes = B * ctx * 4
+    alg_logits = key_bytes + logit_bytes + B * 64 * 128 + B * 64 * 4 + B * nb_per * 4
+    alg_topk = logit_bytes + B * topk * 4
+    peaks = _peaks()
+    achieved = alg_logits / (times["logits"] * 1e-3) / 1e9
+    roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"] + " (burst)",
+            "kernel": "indexer_logits_kernel", "time_source": "back-to-back window of logits calls",
+            "kernel_us": times["logits"] * 1e3,
+            "traffic": _traffic_per_launch("indexer_logits_kernel", "idx"),
+            "algorithmic_bytes_per_launch": alg_logits}
+    return {
+        "metric": "DSA indexer fp8 paged MQA logits + top-k, B=64, 64 heads x 128, ctx 32768, top-2048",
+        "value": key_bytes / (times["both"] * 1e-3) / 1e9, "unit": "GB/s (index keys)",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": times["both"],
+        "us_per_call": times["both"] * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e4m3 MMA, f32 accumulate", "data": "synthetic",
+        "config": {"workload": "idx: B=64 next_n=1 H=64 D=128 ctx=32768 topk=2048 page=64",
+                   "l2": f"{N_SETS} rotating query sets over {key_bytes / 1e6:.0f} MB of keys > 126 MB L2"},
+        "logits_us": times["logits"] * 1e3, "topk_us": times["topk"] * 1e3,
+        "roofline": roof, "gpu_launches": 2 * args.steps, "clocks": clk.summary(),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5"])
+    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5", "idx"],
+                    help="c2-c5: the decode shapes; idx: the DSA indexer read path (one GPU)")
     ap.add_argument("--requests", type=int, default=0,
                     help="per-GPU batch override for profiling a smaller case (0 = the workload's)")
     ap.add_argument("--cpu-sample", type=int, default=8,
@@ -474,6 +559,10 @@ def main():
             print(json.dumps(line), flush=True)
         return
 
+    if args.workload == "idx":
+        if rank == 0:
+            print(json.dumps(run_indexer(args)), flush=True)
+        return
     line = run_ours(args, rank, world, local_rank)
     if rank == 0 and line is not None:
         if world == 1 and not args.no_cpu_baseline:

@@ -148,3 +148,15 @@ def test_indexer_topk_feeds_the_paged_decode(cuda_device):
     ref, _ = O.sparse_decode(synthetic.bf16_to_f32(wk.q_bits), pool.view(-1, 656).cpu().numpy(),
                              slots, wk.sm_scale)
     U.assert_close(out.float().cpu().numpy(), ref)
+
+
+def test_indexer_topk_rows_longer_than_the_resident_limit(cuda_device):
+    """Rows above 48 K positions select from global memory (the other code
+    path of the top-k kernel): same result as the oracle, ties included."""
+    rng = np.random.default_rng(10)
+    L = 70000
+    lg = rng.standard_normal((2, L)).astype(np.float32)
+    lg[0, ::3] = 0.5  # a large tie class near the threshold
+    ctx = np.array([L, 65000], np.int32)
+    top = indexer_topk(torch.from_numpy(lg).cuda(), 1, torch.from_numpy(ctx).cuda(), 2048).cpu().numpy()
+    assert np.array_equal(top, O.indexer_topk(lg, 1, ctx, 2048))

@@ -30,9 +30,10 @@
 // the MMAs of tile t+1.  Every wait is bounded (status word, as the decode).
 //
 // Top-k kernel: one CTA per logits row.  Logits map to order-preserving
-// 32-bit keys; three histogram passes (11, 11 and 10 bits) find the k-th
-// largest key exactly; a final pass in position order writes every position
-// above it and the lowest-positioned ties, ascending, then -1 padding.
+// 32-bit keys (kept in shared memory for rows of up to 48 K positions); three
+// histogram passes (11, 11 and 10 bits) find the k-th largest key exactly; a
+// final pass in position order writes every position above it and the
+// lowest-positioned ties, ascending, then -1 padding.
 #include "common.cuh"
 #include "decode.h"
 #include "tc_ptx.cuh"
@@ -357,9 +358,16 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* warp_s
   return before;
 }
 
+// Rows of up to this many positions keep their keys in shared memory
+// (192 KB), so the row is read from global memory once; longer rows re-read it
+// for each pass (from L2).
+constexpr int kSmemKeys = 48 * 1024;
+
+template <bool kResident>
 __global__ void __launch_bounds__(kTopkThreads)
     indexer_topk_kernel(const float* logits, int64_t logits_stride, int next_n, const int32_t* ctx,
                         int32_t* out, int64_t out_stride, int k, int64_t max_len) {
+  extern __shared__ uint32_t skeys[];  // kResident: the row's keys
   __shared__ uint32_t hist[2048];
   __shared__ uint32_t warp_sums[32];
   __shared__ uint32_t sel[2];  // chosen bin, keys above it (this pass)
@@ -374,6 +382,14 @@ __global__ void __launch_bounds__(kTopkThreads)
     for (int i = threadIdx.x; i < k; i += kTopkThreads) o[i] = i < lim ? i : -1;
     return;
   }
+  if constexpr (kResident) {
+    for (int64_t i = threadIdx.x; i < lim; i += kTopkThreads) skeys[i] = sortable_key(row[i]);
+    __syncthreads();
+  }
+  auto key_at = [&](int64_t i) -> uint32_t {
+    if constexpr (kResident) return skeys[i];
+    return sortable_key(row[i]);
+  };
   // radix select of the k-th largest key: 11 + 11 + 10 bits
   uint32_t prefix = 0, pmask = 0, remaining = (uint32_t)k;
 #pragma unroll 1
@@ -383,7 +399,7 @@ __global__ void __launch_bounds__(kTopkThreads)
     for (int i = threadIdx.x; i < nbins; i += kTopkThreads) hist[i] = 0;
     __syncthreads();
     for (int64_t i = threadIdx.x; i < lim; i += kTopkThreads) {
-      const uint32_t key = sortable_key(row[i]);
+      const uint32_t key = key_at(i);
       if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & (nbins - 1)], 1u);
     }
     __syncthreads();
@@ -400,8 +416,7 @@ __global__ void __launch_bounds__(kTopkThreads)
         if (lane >= o2) incl += y;
       }
       const uint32_t excl = incl - sum;
-      const bool mine = excl < remaining && incl >= remaining;
-      if (mine) {
+      if (excl < remaining && incl >= remaining) {
         uint32_t above = excl;
         int bi = hi - 1;
         for (; bi > hi - per; --bi) {
@@ -428,8 +443,8 @@ __global__ void __launch_bounds__(kTopkThreads)
     uint32_t cg = 0, ce = 0;
 #pragma unroll
     for (int j = 0; j < kItems; ++j) {
-      keys[j] = (i0 + j < lim) ? sortable_key(row[i0 + j]) : 0u;
       const bool valid = i0 + j < lim;
+      keys[j] = valid ? key_at(i0 + j) : 0u;
       cg += (valid && keys[j] > prefix) ? 1u : 0u;
       ce += (valid && keys[j] == prefix) ? 1u : 0u;
     }
@@ -510,9 +525,20 @@ int launch_indexer_logits(const uint8_t* q, int64_t B, int64_t next_n, int64_t q
 int launch_indexer_topk(const float* logits, int64_t rows, int64_t logits_stride, int64_t next_n,
                         const int32_t* ctx, int32_t* out, int64_t out_stride, int64_t topk,
                         int64_t max_len, cudaStream_t st) {
-  return check_cuda(launch_pdl(idx::indexer_topk_kernel, dim3((unsigned)rows), dim3(idx::kTopkThreads),
-                               0, st, logits, logits_stride, (int)next_n, ctx, out, out_stride,
-                               (int)topk, max_len),
+  if (max_len <= idx::kSmemKeys) {
+    const size_t smem = (size_t)max_len * sizeof(uint32_t);
+    cudaError_t e = cudaFuncSetAttribute(idx::indexer_topk_kernel<true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(idx::kSmemKeys * sizeof(uint32_t)));
+    if (e != cudaSuccess) return check_cuda(e, "indexer top-k smem attribute");
+    return check_cuda(launch_pdl(idx::indexer_topk_kernel<true>, dim3((unsigned)rows),
+                                 dim3(idx::kTopkThreads), smem, st, logits, logits_stride,
+                                 (int)next_n, ctx, out, out_stride, (int)topk, max_len),
+                      "indexer_topk_kernel launch");
+  }
+  return check_cuda(launch_pdl(idx::indexer_topk_kernel<false>, dim3((unsigned)rows),
+                               dim3(idx::kTopkThreads), 0, st, logits, logits_stride, (int)next_n,
+                               ctx, out, out_stride, (int)topk, max_len),
                     "indexer_topk_kernel launch");
 }
 
