@@ -13,6 +13,9 @@ MIN_COS = 0.9999
 # precision) the only remaining differences are P's bf16 rounding and
 # accumulation order.
 MAX_ABS_KERNEL_ROUNDING = 5e-3
+# Split-KV partials are stored as bf16 before the merge: one more rounding of a
+# value of the output's size, at most one bf16 ulp (2^-8 relative).
+BF16_ULP = 2.0 ** -8
 
 
 def bf16_tensor(bits: np.ndarray, device="cuda") -> torch.Tensor:
@@ -43,6 +46,22 @@ def assert_close(out, ref, max_abs=MAX_ABS, min_cos=MIN_COS, what="out"):
     m, c = O.max_abs(out, ref), O.cosine(out, ref)
     assert m <= max_abs and c >= min_cos, f"{what}: max_abs={m:.3e} cosine={c:.6f}"
     return m, c
+
+
+def assert_close_rounded(out, ko, what="out"):
+    """Kernel output vs the oracle with tensor-core operand rounding: within
+    MAX_ABS_KERNEL_ROUNDING plus one bf16 rounding of each value (the split
+    partial's), cosine >= MIN_COS."""
+    out = np.asarray(out, np.float64)
+    ko = np.asarray(ko, np.float64)
+    assert np.isfinite(out).all(), f"{what}: non-finite values"
+    err = np.abs(out - ko)
+    bound = MAX_ABS_KERNEL_ROUNDING + BF16_ULP * np.abs(ko)
+    i = np.unravel_index(int(np.argmax(err - bound)), err.shape)
+    c = O.cosine(out, ko)
+    assert (err <= bound).all() and c >= MIN_COS, \
+        f"{what}: |err| {err[i]:.3e} > {bound[i]:.3e} at {i} (|ref| {abs(ko[i]):.3f}), cosine={c:.6f}"
+    return float(err.max()), c
 
 
 def assert_lse_close(lse, ref, max_abs=MAX_ABS):
