@@ -349,10 +349,10 @@ def test_dispatch_by_heads_and_dtype(cuda_device):
     # automatic split count doubles to 2
     assert decode_kernel_name(32, 64, 1, 2048) == "decode_tc3_kernel+merge_splits_kernel"
     assert decode_kernel_name(64, 128, 1, 2048, torch.float32) == "decode_mma_kernel"
-    # small head counts with bf16 q: the persistent swapped-orientation tcgen05 kernel
+    # small head counts with bf16 q: the persistent TMA-gather warp-MMA kernel
     assert decode_kernel_name(256, 16, 1, 2048, torch.bfloat16, 8) == \
-        "decode_sh_kernel+merge_splits_kernel"
-    assert decode_kernel_name(4, 8, 2, 256, torch.bfloat16, 1) == "decode_sh_kernel"
+        "decode_ws_kernel+merge_splits_kernel"
+    assert decode_kernel_name(4, 8, 2, 256, torch.bfloat16, 1) == "decode_ws_kernel"
     assert decode_kernel_name(4, 16, 1, 256, torch.float32, 1) == "decode_mma_kernel"
 
 

@@ -63,13 +63,13 @@ def test_selftest_rejects_iteration_counts_outside_the_limit(cuda_device):
 
 
 def test_small_head_decode_timeout_path_returns_and_reports(cuda_device):
-    """Drive decode_sh_kernel's own error path: with a hand-off limit of two
+    """Drive decode_ws_kernel's own error path: with a hand-off limit of two
     try_wait calls its waits give up while rows are still arriving.  The
-    producer then stops issuing copies, waits for the ones it issued, the MMA
-    issuer drains its MMAs, and every warp returns: the call completes, the
-    status word carries the timeout bit with the small-head kernel's wait codes
-    (16-31, OR-ed together when several waits gave up, so within [16, 32)), and
-    after restoring the limit the same context decodes correctly."""
+    producers then stop issuing copies, wait for the ones they issued, and every
+    warp returns: the call completes, the status word carries the timeout bit
+    with the small-head kernel's wait codes (20-27, OR-ed together when several
+    waits gave up, so within [16, 32)), and after restoring the limit the same
+    context decodes correctly."""
     L = N.lib()
     s = synthetic.Shape("fdws", B=16, H=16, topk=1024, ctx=4096, pool_slots=16 * 4096,
                         mask_frac=0.1)

@@ -134,12 +134,12 @@ def test_fp32_q_kernel_offsets_past_2_31(c4_pool, H):
 
 
 def test_small_head_kernel_offsets_past_2_31_on_c4_pool(c4_pool):
-    """decode_sh_kernel (TMA gather4 rows, swapped tcgen05 MMAs) on the same top rows."""
+    """decode_ws_kernel (TMA gather4 rows) on the same top rows."""
     w = c4_pool
     n = w.kv.view(-1, 656).shape[0]
     slots = _place_past_boundary(w.slots[:3], n, np.random.default_rng(5))
     q = torch.randn((3, 16, 576), generator=torch.Generator().manual_seed(5)).bfloat16().cuda()
-    assert decode_kernel_name(3, 16, 1, 2048, torch.bfloat16, 4).startswith("decode_sh_kernel")
+    assert decode_kernel_name(3, 16, 1, 2048, torch.bfloat16, 4).startswith("decode_ws_kernel")
     out, lse = fp8_ds_mla_sparse_decode(q, w.kv, slots, w.sm_scale, return_lse=True, num_kv_splits=4)
     _check_requests(out, lse, q, w.kv, slots, w.sm_scale, range(3))
 

@@ -22,7 +22,7 @@ OUT_DIR = os.path.join(HERE, "vllm_fp8kv")
 LIB = os.path.join(OUT_DIR, "libfp8mla.so")
 OBJ_DIR = os.path.join(HERE, "_build")
 SOURCES = ["abi.cu", "abi_noalloc.cu", "unit_kernels.cu", "decode_mma.cu", "decode_tc3.cu",
-           "decode_sh.cu", "decode_ws.cu", "tma_map.cu", "indexer.cu"]
+           "decode_ws.cu", "tma_map.cu", "indexer.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

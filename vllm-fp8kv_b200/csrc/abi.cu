@@ -130,12 +130,11 @@ int fp8mla_device_status(unsigned int* status, int reset, void* stream) {
   *status = 0;
   if (int rc = require_sm100()) return rc;
   // each kernel file keeps its own status word
-  unsigned int v1 = 0, v2 = 0, v3 = 0, v4 = 0;
-  int rc = read_device_status_sh(&v1, reset != 0, static_cast<cudaStream_t>(stream));
-  if (rc == FP8MLA_OK) rc = read_device_status_ws(&v2, reset != 0, static_cast<cudaStream_t>(stream));
+  unsigned int v2 = 0, v3 = 0, v4 = 0;
+  int rc = read_device_status_ws(&v2, reset != 0, static_cast<cudaStream_t>(stream));
   if (rc == FP8MLA_OK) rc = read_device_status_tc3(&v3, reset != 0, static_cast<cudaStream_t>(stream));
   if (rc == FP8MLA_OK) rc = read_device_status_idx(&v4, reset != 0, static_cast<cudaStream_t>(stream));
-  *status = v1 | v2 | v3 | v4;
+  *status = v2 | v3 | v4;
   return rc;
 }
 
@@ -192,11 +191,8 @@ const char* fp8mla_decode_kernel_name(int64_t T, int64_t H, int64_t G, int64_t t
   a.hpg = (int)(H / G);
   a.block_h = a.hpg < 16 ? a.hpg : 16;
   a.num_slots = 1;  // names the kernel of a non-empty pool
-  a.q_sh = kDqk;    // and of contiguous queries
-  a.q_st = H * kDqk;
   a.num_splits = S < 1 ? 1 : S;
   const char* k = decode_tc3_supported(a)  ? "decode_tc3_kernel"
-                  : decode_sh_supported(a) ? "decode_sh_kernel"
                   : decode_ws_supported(a) ? "decode_ws_kernel"
                                            : "decode_mma_kernel";
   if (a.num_splits == 1) return k;
@@ -302,7 +298,6 @@ int decode_impl(const void* q, int q_dtype, int64_t T, int64_t H, int64_t q_stri
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (decode_tc3_supported(a)) return launch_decode_tc3(a, st);
-  if (decode_sh_supported(a)) return launch_decode_sh(a, device_sm_count(), st);
   if (decode_ws_supported(a)) return launch_decode_ws(a, device_sm_count(), st);
   return launch_decode_mma(a, st);
 }

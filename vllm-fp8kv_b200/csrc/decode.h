@@ -128,9 +128,6 @@ int launch_wait_timeout_selftest(uint32_t iters, uint64_t* elapsed_ns, cudaStrea
 bool decode_tc3_supported(const DecodeArgs& a);
 int launch_decode_tc3(const DecodeArgs& a, cudaStream_t st);
 int read_device_status_tc3(unsigned int* status, bool reset, cudaStream_t st);
-bool decode_sh_supported(const DecodeArgs& a);
-int launch_decode_sh(const DecodeArgs& a, int sms, cudaStream_t st);
-int read_device_status_sh(unsigned int* status, bool reset, cudaStream_t st);
 bool decode_ws_supported(const DecodeArgs& a);
 int launch_decode_ws(const DecodeArgs& a, int sms, cudaStream_t st);
 int read_device_status_ws(unsigned int* status, bool reset, cudaStream_t st);

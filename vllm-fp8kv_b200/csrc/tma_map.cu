@@ -57,21 +57,4 @@ int encode_indexer_page_map(CUtensorMap* tm, const uint8_t* k_cache, int64_t num
   return FP8MLA_OK;
 }
 
-int encode_q_map(CUtensorMap* tm, const void* q, int64_t T, int64_t H, int64_t q_stride_t,
-                 int64_t q_stride_h) {
-  EncodeTiledFn enc = encode_fn();
-  if (enc == nullptr) return set_error(FP8MLA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  // a single token's stride is never used: give it a valid value
-  const int64_t st = T > 1 ? q_stride_t : H * q_stride_h;
-  const cuuint64_t dims[3] = {(cuuint64_t)kDqk, (cuuint64_t)H, (cuuint64_t)T};
-  const cuuint64_t strides[2] = {(cuuint64_t)q_stride_h * 2, (cuuint64_t)st * 2};
-  const cuuint32_t box[3] = {64, 16, 1};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides,
-                         box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(FP8MLA_ERR_CUDA, "query tensor map encode failed (%d)", (int)r);
-  return FP8MLA_OK;
-}
-
 }  // namespace fp8mla

@@ -24,24 +24,7 @@ int encode_row_map(CUtensorMap* tm, const uint8_t* kv, int64_t num_slots, uint32
 int encode_indexer_page_map(CUtensorMap* tm, const uint8_t* k_cache, int64_t num_blocks,
                             int64_t block_size, int64_t head_dim);
 
-// Encodes `tm` over bf16 queries q[T][H][576] (row strides in elements, 16-B
-// multiples): one box = 16 heads x 64 dims of one token, written into shared
-// memory with the 128-byte swizzle of a K-major operand (heads past H read as
-// zeros).
-int encode_q_map(CUtensorMap* tm, const void* q, int64_t T, int64_t H, int64_t q_stride_t,
-                 int64_t q_stride_h);
-
 #ifdef __CUDACC__
-// One box of a 3-D map at (x, y, z) -> shared address dst; completion counted
-// on `bar`.
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* tm, int32_t x,
-                                            int32_t y, int32_t z, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(dst),
-      "l"(tm), "r"(x), "r"(y), "r"(z), "r"(bar)
-      : "memory");
-}
 // Four rows r0..r3 of `tm` at column x (in uint64 words) -> 4 consecutive
 // box-wide rows at shared address dst; completion counted on `bar`.
 __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* tm, int32_t x,
