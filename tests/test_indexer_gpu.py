@@ -160,3 +160,16 @@ def test_indexer_topk_rows_longer_than_the_resident_limit(cuda_device):
     ctx = np.array([L, 65000], np.int32)
     top = indexer_topk(torch.from_numpy(lg).cuda(), 1, torch.from_numpy(ctx).cuda(), 2048).cpu().numpy()
     assert np.array_equal(top, O.indexer_topk(lg, 1, ctx, 2048))
+
+
+def test_indexer_topk_row_in_one_first_pass_bin(cuda_device):
+    """Every logit in [1, 1.25) shares the first pass's 11-bit bin, more keys
+    than the compacted candidate list holds: the refining passes then scan the
+    whole row.  Ties (values on a 1/4096 grid) resolve to the lower positions."""
+    rng = np.random.default_rng(12)
+    L = 32768
+    lg = (1.0 + rng.integers(0, 1024, size=(3, L)) / 4096.0).astype(np.float32)
+    lg[2, :5000] = 1.0  # a tie class at the bottom
+    ctx = np.array([L, 30000, L], np.int32)
+    top = indexer_topk(torch.from_numpy(lg).cuda(), 1, torch.from_numpy(ctx).cuda(), 2048).cpu().numpy()
+    assert np.array_equal(top, O.indexer_topk(lg, 1, ctx, 2048))

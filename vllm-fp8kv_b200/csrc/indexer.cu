@@ -362,6 +362,9 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* warp_s
 // (192 KB), so the row is read from global memory once; longer rows re-read it
 // for each pass (from L2).
 constexpr int kSmemKeys = 48 * 1024;
+constexpr int kCand = 4096;  // compacted candidates of the first pass (16 KB)
+constexpr int64_t kRound = (int64_t)kTopkThreads * 32;  // positions of one write round
+static_assert(kSmemKeys <= 2 * kRound, "resident rows take at most two write rounds");
 
 template <bool kResident>
 __global__ void __launch_bounds__(kTopkThreads)
@@ -371,6 +374,9 @@ __global__ void __launch_bounds__(kTopkThreads)
   __shared__ uint32_t hist[2048];
   __shared__ uint32_t warp_sums[32];
   __shared__ uint32_t sel[2];  // chosen bin, keys above it (this pass)
+  __shared__ uint32_t cand[kCand];  // the first pass's chosen-bin keys (resident: positions)
+  __shared__ uint32_t ncand;
+  __shared__ uint32_t gabove[2][32], cgt[2][32], ceq[2][32];  // per round and warp (resident)
   if (threadIdx.x == 0) pdl_launch_dependents();
   pdl_wait();
   const int64_t r = blockIdx.x;
@@ -382,42 +388,218 @@ __global__ void __launch_bounds__(kTopkThreads)
     for (int i = threadIdx.x; i < k; i += kTopkThreads) o[i] = i < lim ? i : -1;
     return;
   }
-  if constexpr (kResident) {
-    for (int64_t i = threadIdx.x; i < lim; i += kTopkThreads) skeys[i] = sortable_key(row[i]);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t lt = (1u << lane) - 1u;
+  // The bin holding the `remaining`-th largest counted key (bins taken from
+  // the top): thread t owns nbins / 1024 bins and one block scan orders the
+  // threads.  Leaves the bin and the count above it in sel[0], sel[1].
+  auto select_bin = [&](int nbins, uint32_t rem) {
+    const int per = nbins / kTopkThreads;
+    const int hi = nbins - per * (int)threadIdx.x;
+    uint32_t sum = 0;
+    for (int bi = hi - 1; bi >= hi - per; --bi) sum += hist[bi];
+    uint32_t tot;
+    const uint32_t ex = block_excl_scan(sum, warp_sums, &tot);
+    if (ex < rem && ex + sum >= rem) {
+      uint32_t above = ex;
+      int bi = hi - 1;
+      for (; bi > hi - per; --bi) {
+        if (above + hist[bi] >= rem) break;
+        above += hist[bi];
+      }
+      sel[0] = (uint32_t)bi;
+      sel[1] = above;
+    }
     __syncthreads();
+  };
+  if constexpr (kResident) {
+    // ---- the row into shared memory (16-byte cp.async copies, all of a
+    // thread's in flight at once; unaligned rows and the ragged tail element
+    // by element), converted to keys in place while the first pass's
+    // histogram (top 11 bits) is counted
+    for (int i = threadIdx.x; i < 2048; i += kTopkThreads) hist[i] = 0;
+    __syncthreads();
+    const int64_t n4 = (reinterpret_cast<uintptr_t>(row) & 15u) == 0 ? lim >> 2 : 0;
+    for (int64_t i = threadIdx.x; i < n4; i += kTopkThreads)
+      cp_async16(smem_u32(&skeys[4 * i]), row + 4 * i, 16);
+    cp_async_commit();
+    for (int64_t i = 4 * n4 + threadIdx.x; i < lim; i += kTopkThreads) {
+      const uint32_t key = sortable_key(row[i]);
+      skeys[i] = key;
+      atomicAdd(&hist[key >> 21], 1u);
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < n4; i += kTopkThreads) {
+      uint4 v = reinterpret_cast<const uint4*>(skeys)[i];
+      v = make_uint4(sortable_key(__uint_as_float(v.x)), sortable_key(__uint_as_float(v.y)),
+                     sortable_key(__uint_as_float(v.z)), sortable_key(__uint_as_float(v.w)));
+      reinterpret_cast<uint4*>(skeys)[i] = v;
+      atomicAdd(&hist[v.x >> 21], 1u);
+      atomicAdd(&hist[v.y >> 21], 1u);
+      atomicAdd(&hist[v.z >> 21], 1u);
+      atomicAdd(&hist[v.w >> 21], 1u);
+    }
+    __syncthreads();
+    uint32_t remaining = (uint32_t)k;
+    select_bin(2048, remaining);
+    const uint32_t bin0 = sel[0];
+    const bool fits = hist[bin0] <= (uint32_t)kCand;  // the bin's keys fit the candidate list
+    uint32_t prefix = bin0 << 21, pmask = 0x7FFu << 21;
+    remaining -= sel[1];
+    // ---- in the write pass's mapping (warp w: positions [1024 w, +1024) of
+    // each 32 K round, lane l position 32 j + l at step j): per warp and
+    // round, the keys above the bin; the bin's positions into the candidates
+    const int rounds = (int)((lim + kRound - 1) / kRound);  // <= 2
+    if (threadIdx.x == 0) ncand = 0;
+    __syncthreads();
+    for (int rd = 0; rd < rounds; ++rd) {
+      const int64_t wb = (int64_t)rd * kRound + (int64_t)warp * 1024;
+      uint32_t ga = 0;
+#pragma unroll 4
+      for (int j = 0; j < 32; ++j) {
+        const int64_t i = wb + 32 * j + lane;
+        const bool v = i < lim;
+        const uint32_t top = v ? skeys[i] >> 21 : 0u;
+        ga += __popc(__ballot_sync(0xFFFFFFFFu, v && top > bin0));
+        if (fits) {
+          const bool m = v && top == bin0;
+          const uint32_t bal = __ballot_sync(0xFFFFFFFFu, m);
+          uint32_t base = 0;
+          if (lane == 0 && bal != 0) base = atomicAdd(&ncand, (uint32_t)__popc(bal));
+          base = __shfl_sync(0xFFFFFFFFu, base, 0);
+          if (m) cand[base + __popc(bal & lt)] = (uint32_t)i;
+        }
+      }
+      if (lane == 0) gabove[rd][warp] = ga;
+    }
+    __syncthreads();
+    // ---- the two refining passes over the bin's keys (or, when they did not
+    // fit, over the whole row)
+    const int nc = fits ? (int)ncand : 0;
+#pragma unroll 1
+    for (int pass = 1; pass < 3; ++pass) {
+      const int shift = pass == 1 ? 10 : 0;
+      const int nbins = pass == 2 ? 1024 : 2048;
+      for (int i = threadIdx.x; i < nbins; i += kTopkThreads) hist[i] = 0;
+      __syncthreads();
+      if (fits) {
+        for (int c = threadIdx.x; c < nc; c += kTopkThreads) {
+          const uint32_t key = skeys[cand[c]];
+          if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & (nbins - 1)], 1u);
+        }
+      } else {
+        for (int64_t i = threadIdx.x; i < lim; i += kTopkThreads) {
+          const uint32_t key = skeys[i];
+          if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & (nbins - 1)], 1u);
+        }
+      }
+      __syncthreads();
+      select_bin(nbins, remaining);
+      prefix |= sel[0] << shift;
+      pmask |= (uint32_t)(nbins - 1) << shift;
+      remaining -= sel[1];
+      __syncthreads();  // sel and hist are rewritten by the next pass
+    }
+    // ---- per warp and round, keys above the k-th key and keys equal to it:
+    // the bin's share from the candidates, or a counting pass over the row
+    if (threadIdx.x < 2 * 32) {
+      cgt[threadIdx.x >> 5][threadIdx.x & 31] = 0;
+      ceq[threadIdx.x >> 5][threadIdx.x & 31] = 0;
+    }
+    __syncthreads();
+    if (fits) {
+      for (int c = threadIdx.x; c < nc; c += kTopkThreads) {
+        const uint32_t pos = cand[c], key = skeys[pos];
+        const int rd = (int)(pos / kRound), ww = (int)((pos % kRound) >> 10);
+        if (key > prefix) atomicAdd(&cgt[rd][ww], 1u);
+        else if (key == prefix) atomicAdd(&ceq[rd][ww], 1u);
+      }
+    } else {
+      for (int rd = 0; rd < rounds; ++rd) {
+        const int64_t wb = (int64_t)rd * kRound + (int64_t)warp * 1024;
+        uint32_t cg = 0, ce = 0;
+#pragma unroll 4
+        for (int j = 0; j < 32; ++j) {
+          const int64_t i = wb + 32 * j + lane;
+          const uint32_t key = i < lim ? skeys[i] : 0u;
+          cg += __popc(__ballot_sync(0xFFFFFFFFu, i < lim && key > prefix && (key >> 21) == bin0));
+          ce += __popc(__ballot_sync(0xFFFFFFFFu, i < lim && key == prefix));
+        }
+        if (lane == 0) {
+          cgt[rd][warp] = cg;
+          ceq[rd][warp] = ce;
+        }
+      }
+    }
+    __syncthreads();
+    // ---- write: ascending positions above the k-th key and the first
+    // `remaining` equal to it, then nothing else (lim > k: exactly k)
+    uint32_t base_g = 0, base_e = 0;
+    for (int rd = 0; rd < rounds; ++rd) {
+      const int64_t wb = (int64_t)rd * kRound + (int64_t)warp * 1024;
+      const uint32_t cg = gabove[rd][warp] + cgt[rd][warp], ce = ceq[rd][warp];
+      uint32_t tot;
+      const uint32_t ex = block_excl_scan(lane == 0 ? ((cg << 16) | ce) : 0u, warp_sums, &tot);
+      const uint32_t exw = __shfl_sync(0xFFFFFFFFu, ex, 0);
+      uint32_t g = base_g + (exw >> 16), e = base_e + (exw & 0xFFFFu);
+#pragma unroll 4
+      for (int j = 0; j < 32; ++j) {
+        const int64_t i = wb + 32 * j + lane;
+        const uint32_t key = i < lim ? skeys[i] : 0u;
+        const bool isg = i < lim && key > prefix, ise = i < lim && key == prefix;
+        const uint32_t bg = __ballot_sync(0xFFFFFFFFu, isg), be = __ballot_sync(0xFFFFFFFFu, ise);
+        const uint32_t gb = g + __popc(bg & lt), eb = e + __popc(be & lt);
+        if (isg) o[gb + min(eb, remaining)] = (int32_t)i;
+        else if (ise && eb < remaining) o[gb + eb] = (int32_t)i;
+        g += __popc(bg);
+        e += __popc(be);
+      }
+      base_g += tot >> 16;
+      base_e += tot & 0xFFFFu;
+    }
+    return;
   }
+  // ===== rows above the resident limit: every pass reads the row (from L2)
   auto key_at = [&](int64_t i) -> uint32_t {
     if constexpr (kResident) return skeys[i];
     return sortable_key(row[i]);
   };
-  // radix select of the k-th largest key: 11 + 11 + 10 bits
+  // radix select of the k-th largest key: 11 + 11 + 10 bits.  After the first
+  // pass the keys of the chosen bin (usually a few percent of the row) are
+  // compacted, and the later passes count only them; a bin of more than
+  // kCand keys keeps the full scans.
   uint32_t prefix = 0, pmask = 0, remaining = (uint32_t)k;
+  bool use_cand = false;
 #pragma unroll 1
   for (int pass = 0; pass < 3; ++pass) {
     const int shift = pass == 0 ? 21 : pass == 1 ? 10 : 0;
     const int nbins = pass == 2 ? 1024 : 2048;
     for (int i = threadIdx.x; i < nbins; i += kTopkThreads) hist[i] = 0;
     __syncthreads();
-    for (int64_t i = threadIdx.x; i < lim; i += kTopkThreads) {
-      const uint32_t key = key_at(i);
-      if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & (nbins - 1)], 1u);
+    if (use_cand) {
+      for (int i = threadIdx.x; i < (int)ncand; i += kTopkThreads) {
+        const uint32_t key = cand[i];
+        if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & (nbins - 1)], 1u);
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < lim; i += kTopkThreads) {
+        const uint32_t key = key_at(i);
+        if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & (nbins - 1)], 1u);
+      }
     }
     __syncthreads();
-    if (threadIdx.x < 32) {
-      // lane l owns bins [nbins - per*(l+1), nbins - per*l), scanned from the top
-      const int lane = threadIdx.x, per = nbins / 32;
-      const int hi = nbins - per * lane;
+    // the bin holding the remaining-th largest key: thread t owns `per` bins,
+    // taken from the top, and one block scan orders the threads
+    {
+      const int per = nbins / kTopkThreads;
+      const int hi = nbins - per * (int)threadIdx.x;
       uint32_t sum = 0;
       for (int bi = hi - 1; bi >= hi - per; --bi) sum += hist[bi];
-      uint32_t incl = sum;
-#pragma unroll
-      for (int o2 = 1; o2 < 32; o2 <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o2);
-        if (lane >= o2) incl += y;
-      }
-      const uint32_t excl = incl - sum;
-      if (excl < remaining && incl >= remaining) {
-        uint32_t above = excl;
+      uint32_t tot;
+      const uint32_t ex = block_excl_scan(sum, warp_sums, &tot);
+      if (ex < remaining && ex + sum >= remaining) {
+        uint32_t above = ex;
         int bi = hi - 1;
         for (; bi > hi - per; --bi) {
           if (above + hist[bi] >= remaining) break;
@@ -428,39 +610,60 @@ __global__ void __launch_bounds__(kTopkThreads)
       }
     }
     __syncthreads();
-    prefix |= sel[0] << shift;
+    const uint32_t bin = sel[0];
+    prefix |= bin << shift;
     pmask |= (uint32_t)(nbins - 1) << shift;
     remaining -= sel[1];
-    __syncthreads();  // sel and hist are rewritten by the next pass
+    if (pass == 0 && hist[bin] <= (uint32_t)kCand) {
+      // compact the chosen bin's keys (warp-aggregated appends)
+      if (threadIdx.x == 0) ncand = 0;
+      __syncthreads();
+      const int lane = threadIdx.x & 31;
+      const int64_t nr = (lim + 31) & ~(int64_t)31;
+      for (int64_t i = threadIdx.x; i < nr; i += kTopkThreads) {
+        const uint32_t key = i < lim ? key_at(i) : 0u;
+        const bool m = i < lim && (key & pmask) == prefix;
+        const uint32_t bal = __ballot_sync(0xFFFFFFFFu, m);
+        uint32_t base = 0;
+        if (lane == 0 && bal != 0) base = atomicAdd(&ncand, (uint32_t)__popc(bal));
+        base = __shfl_sync(0xFFFFFFFFu, base, 0);
+        if (m) cand[base + __popc(bal & ((1u << lane) - 1u))] = key;
+      }
+      use_cand = true;
+    }
+    __syncthreads();  // sel, hist and the candidates are read by the next pass
   }
   // prefix is the k-th largest key; `remaining` of the keys equal to it are
-  // kept (the lowest positions), every key above it too
+  // kept (the lowest positions), every key above it too.  Warp w takes
+  // positions [1024 w, 1024 w + 1024) of each round, lane l position 32 j + l
+  // at step j (coalesced reads); ballots order the lanes, one block scan the
+  // warps.
   uint32_t base_g = 0, base_e = 0;
-  constexpr int kItems = 4;
-  for (int64_t start = 0; start < lim; start += (int64_t)kTopkThreads * kItems) {
-    const int64_t i0 = start + (int64_t)threadIdx.x * kItems;
-    uint32_t keys[kItems];
+  for (int64_t start = 0; start < lim; start += kRound) {
+    const int64_t wb = start + (int64_t)warp * 1024;
     uint32_t cg = 0, ce = 0;
-#pragma unroll
-    for (int j = 0; j < kItems; ++j) {
-      const bool valid = i0 + j < lim;
-      keys[j] = valid ? key_at(i0 + j) : 0u;
-      cg += (valid && keys[j] > prefix) ? 1u : 0u;
-      ce += (valid && keys[j] == prefix) ? 1u : 0u;
+#pragma unroll 4
+    for (int j = 0; j < 32; ++j) {
+      const int64_t i = wb + 32 * j + lane;
+      const uint32_t key = i < lim ? key_at(i) : 0u;
+      cg += __popc(__ballot_sync(0xFFFFFFFFu, i < lim && key > prefix));
+      ce += __popc(__ballot_sync(0xFFFFFFFFu, i < lim && key == prefix));
     }
     uint32_t tot;
-    const uint32_t ex = block_excl_scan((cg << 16) | ce, warp_sums, &tot);
-    uint32_t g = base_g + (ex >> 16), e = base_e + (ex & 0xFFFFu);
-#pragma unroll
-    for (int j = 0; j < kItems; ++j) {
-      if (i0 + j >= lim) break;
-      if (keys[j] > prefix) {
-        o[g + min(e, remaining)] = (int32_t)(i0 + j);
-        ++g;
-      } else if (keys[j] == prefix) {
-        if (e < remaining) o[g + e] = (int32_t)(i0 + j);
-        ++e;
-      }
+    const uint32_t ex = block_excl_scan(lane == 0 ? ((cg << 16) | ce) : 0u, warp_sums, &tot);
+    const uint32_t exw = __shfl_sync(0xFFFFFFFFu, ex, 0);
+    uint32_t g = base_g + (exw >> 16), e = base_e + (exw & 0xFFFFu);
+#pragma unroll 4
+    for (int j = 0; j < 32; ++j) {
+      const int64_t i = wb + 32 * j + lane;
+      const uint32_t key = i < lim ? key_at(i) : 0u;
+      const bool isg = i < lim && key > prefix, ise = i < lim && key == prefix;
+      const uint32_t bg = __ballot_sync(0xFFFFFFFFu, isg), be = __ballot_sync(0xFFFFFFFFu, ise);
+      const uint32_t gb = g + __popc(bg & lt), eb = e + __popc(be & lt);
+      if (isg) o[gb + min(eb, remaining)] = (int32_t)i;
+      else if (ise && eb < remaining) o[gb + eb] = (int32_t)i;
+      g += __popc(bg);
+      e += __popc(be);
     }
     base_g += tot >> 16;
     base_e += tot & 0xFFFFu;
