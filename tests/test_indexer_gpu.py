@@ -151,8 +151,8 @@ def test_indexer_topk_feeds_the_paged_decode(cuda_device):
 
 
 def test_indexer_topk_rows_longer_than_the_resident_limit(cuda_device):
-    """Rows above 48 K positions select from global memory (the other code
-    path of the top-k kernel): same result as the oracle, ties included."""
+    """Rows above 48 K positions take two write rounds in each CTA of the
+    pair: same result as the oracle, ties included."""
     rng = np.random.default_rng(10)
     L = 70000
     lg = rng.standard_normal((2, L)).astype(np.float32)
@@ -171,5 +171,17 @@ def test_indexer_topk_row_in_one_first_pass_bin(cuda_device):
     lg = (1.0 + rng.integers(0, 1024, size=(3, L)) / 4096.0).astype(np.float32)
     lg[2, :5000] = 1.0  # a tie class at the bottom
     ctx = np.array([L, 30000, L], np.int32)
+    top = indexer_topk(torch.from_numpy(lg).cuda(), 1, torch.from_numpy(ctx).cuda(), 2048).cpu().numpy()
+    assert np.array_equal(top, O.indexer_topk(lg, 1, ctx, 2048))
+
+
+def test_indexer_topk_rows_above_the_pair_limit(cuda_device):
+    """Rows of more than 96,256 positions take the single-CTA kernel that
+    re-reads the row per pass; a short row in the same call leaves early."""
+    rng = np.random.default_rng(14)
+    L = 100000
+    lg = rng.standard_normal((2, L)).astype(np.float32)
+    lg[0, ::7] = 0.25  # a tie class
+    ctx = np.array([L, 1500], np.int32)
     top = indexer_topk(torch.from_numpy(lg).cuda(), 1, torch.from_numpy(ctx).cuda(), 2048).cpu().numpy()
     assert np.array_equal(top, O.indexer_topk(lg, 1, ctx, 2048))

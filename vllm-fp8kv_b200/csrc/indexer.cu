@@ -36,6 +36,7 @@
 // lowest-positioned ties, ascending, then -1 padding.
 #include "common.cuh"
 #include "decode.h"
+#include "tc_cluster.cuh"
 #include "tc_ptx.cuh"
 #include "tma_map.h"
 
@@ -358,25 +359,267 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* warp_s
   return before;
 }
 
-// Rows of up to this many positions keep their keys in shared memory
-// (192 KB), so the row is read from global memory once; longer rows re-read it
-// for each pass (from L2).
+// A row is split over a 2-CTA cluster; each CTA keeps up to this many of its
+// positions' keys in shared memory (192 KB), so the row is read from global
+// memory once.  Longer rows take the single-CTA kernel, which re-reads the
+// row for each pass (from L2).
 constexpr int kSmemKeys = 48 * 1024;
 constexpr int kCand = 4096;  // compacted candidates of the first pass (16 KB)
 constexpr int64_t kRound = (int64_t)kTopkThreads * 32;  // positions of one write round
-static_assert(kSmemKeys <= 2 * kRound, "resident rows take at most two write rounds");
+static_assert(kSmemKeys <= 2 * kRound, "a CTA's positions take at most two write rounds");
 
-template <bool kResident>
+// Positions of a row per CTA of the pair: half the row, rounded up to whole
+// 1024-position warp ranges; CTA c takes [c * half, c * half + half).
+__host__ __device__ constexpr int64_t pair_half(int64_t lim) {
+  return (((lim + 1) / 2) + 1023) & ~(int64_t)1023;
+}
+// Longest row the pair keeps resident.
+constexpr int64_t kPairMaxLen = 2 * (int64_t)kSmemKeys - 2048;
+static_assert(pair_half(kPairMaxLen) <= kSmemKeys, "");
+
+// A 32-bit word at shared::cta address `local` of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t ld_dsmem(uint32_t local, uint32_t rank) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(mapa(local, rank)) : "memory");
+  return v;
+}
+
+// Top-k of one row on a CTA pair (rows up to kPairMaxLen).  Each CTA loads and
+// converts its half of the row; the three histogram passes add the two CTAs'
+// counts through distributed shared memory, so both choose the same bins;
+// each CTA compacts and counts its own candidates; CTA 1 writes its positions
+// after CTA 0's (its base is CTA 0's totals).
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
+    indexer_topk_pair_kernel(const float* logits, int64_t logits_stride, int next_n,
+                             const int32_t* ctx, int32_t* out, int64_t out_stride, int k,
+                             int64_t max_len) {
+  extern __shared__ uint32_t skeys[];  // keys of this CTA's positions
+  __shared__ uint32_t hist[2048];      // this CTA's counts
+  __shared__ uint32_t hsum[2048];      // both CTAs' counts
+  __shared__ uint32_t warp_sums[32];
+  __shared__ uint32_t sel[2];          // chosen bin, keys above it (this pass)
+  __shared__ uint32_t cand[kCand];     // this CTA's positions in the first pass's bin
+  __shared__ uint32_t ncand;
+  __shared__ uint32_t gabove[32], cgt[32], ceq[32];  // per warp range
+  __shared__ uint32_t tot_ge[2];       // this CTA's keys above / equal to the k-th key
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t peer = cluster_rank() ^ 1u;
+  const int64_t r = blockIdx.x >> 1;
+  const int b = (int)(r / next_n), n = (int)(r % next_n);
+  const int64_t lim = min(max_len, (int64_t)ctx[b] - next_n + n + 1);
+  const float* row = logits + r * logits_stride;
+  int32_t* o = out + r * out_stride;
+  if (lim <= k) {  // every position kept, then padding (both CTAs leave here)
+    if (peer == 1)
+      for (int i = threadIdx.x; i < k; i += kTopkThreads) o[i] = i < lim ? i : -1;
+    return;
+  }
+  const int64_t half = pair_half(lim), base = (int64_t)(peer ^ 1u) * half;
+  const int64_t nloc = max((int64_t)0, min(lim - base, half));  // positions [base, base + nloc)
+  const float* rowl = row + base;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t lt = (1u << lane) - 1u;
+  // both CTAs' counts of the first nbins bins -> hsum (the first barrier: both
+  // histograms are complete; the second: the peer has read this one)
+  auto merge = [&](int nbins) {
+    cluster_sync_all();
+    for (int i = threadIdx.x; i < nbins; i += kTopkThreads)
+      hsum[i] = hist[i] + ld_dsmem(smem_u32(&hist[i]), peer);
+    cluster_sync_all();
+  };
+  // The bin holding the `rem`-th largest counted key (bins taken from the
+  // top): thread t owns nbins / 1024 bins and one block scan orders the
+  // threads.  Leaves the bin and the count above it in sel[0], sel[1].
+  auto select_bin = [&](int nbins, uint32_t rem) {
+    const int per = nbins / kTopkThreads;
+    const int hi = nbins - per * (int)threadIdx.x;
+    uint32_t sum = 0;
+    for (int bi = hi - 1; bi >= hi - per; --bi) sum += hsum[bi];
+    uint32_t tot;
+    const uint32_t ex = block_excl_scan(sum, warp_sums, &tot);
+    if (ex < rem && ex + sum >= rem) {
+      uint32_t above = ex;
+      int bi = hi - 1;
+      for (; bi > hi - per; --bi) {
+        if (above + hsum[bi] >= rem) break;
+        above += hsum[bi];
+      }
+      sel[0] = (uint32_t)bi;
+      sel[1] = above;
+    }
+    __syncthreads();
+  };
+  // ---- this CTA's positions into shared memory (16-byte cp.async copies,
+  // all of a thread's in flight at once; unaligned rows and the ragged tail
+  // element by element), converted to keys in place while the first pass's
+  // histogram (top 11 bits) is counted
+  for (int i = threadIdx.x; i < 2048; i += kTopkThreads) hist[i] = 0;
+  __syncthreads();
+  const int64_t n4 = (reinterpret_cast<uintptr_t>(rowl) & 15u) == 0 ? nloc >> 2 : 0;
+  for (int64_t i = threadIdx.x; i < n4; i += kTopkThreads)
+    cp_async16(smem_u32(&skeys[4 * i]), rowl + 4 * i, 16);
+  cp_async_commit();
+  for (int64_t i = 4 * n4 + threadIdx.x; i < nloc; i += kTopkThreads) {
+    const uint32_t key = sortable_key(rowl[i]);
+    skeys[i] = key;
+    atomicAdd(&hist[key >> 21], 1u);
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < n4; i += kTopkThreads) {
+    uint4 v = reinterpret_cast<const uint4*>(skeys)[i];
+    v = make_uint4(sortable_key(__uint_as_float(v.x)), sortable_key(__uint_as_float(v.y)),
+                   sortable_key(__uint_as_float(v.z)), sortable_key(__uint_as_float(v.w)));
+    reinterpret_cast<uint4*>(skeys)[i] = v;
+    atomicAdd(&hist[v.x >> 21], 1u);
+    atomicAdd(&hist[v.y >> 21], 1u);
+    atomicAdd(&hist[v.z >> 21], 1u);
+    atomicAdd(&hist[v.w >> 21], 1u);
+  }
+  merge(2048);
+  uint32_t remaining = (uint32_t)k;
+  select_bin(2048, remaining);
+  const uint32_t bin0 = sel[0];
+  const bool fits = hist[bin0] <= (uint32_t)kCand;  // this CTA's keys of the bin fit the list
+  uint32_t prefix = bin0 << 21, pmask = 0x7FFu << 21;
+  remaining -= sel[1];
+  // ---- in the write pass's mapping (warp w: local positions [32 S w,
+  // 32 S (w + 1)), lane l position 32 j + l at step j < S): per warp, the
+  // keys above the bin; the bin's positions into the candidates
+  const int S = (int)((nloc + 1023) / 1024);  // steps per warp, <= 48
+  const int64_t wspan = 32 * (int64_t)S;
+  const int64_t wb = (int64_t)warp * wspan;
+  if (threadIdx.x == 0) ncand = 0;
+  __syncthreads();
+  {
+    uint32_t ga = 0;
+#pragma unroll 4
+    for (int j = 0; j < S; ++j) {
+      const int64_t i = wb + 32 * j + lane;
+      const bool v = i < nloc;
+      const uint32_t top = v ? skeys[i] >> 21 : 0u;
+      ga += __popc(__ballot_sync(0xFFFFFFFFu, v && top > bin0));
+      if (fits) {
+        const bool m = v && top == bin0;
+        const uint32_t bal = __ballot_sync(0xFFFFFFFFu, m);
+        uint32_t cb = 0;
+        if (lane == 0 && bal != 0) cb = atomicAdd(&ncand, (uint32_t)__popc(bal));
+        cb = __shfl_sync(0xFFFFFFFFu, cb, 0);
+        if (m) cand[cb + __popc(bal & lt)] = (uint32_t)i;
+      }
+    }
+    if (lane == 0) gabove[warp] = ga;
+  }
+  __syncthreads();
+  // ---- the two refining passes over the bin's keys (or, when this CTA's did
+  // not fit, over its whole half)
+  const int nc = fits ? (int)ncand : 0;
+#pragma unroll 1
+  for (int pass = 1; pass < 3; ++pass) {
+    const int shift = pass == 1 ? 10 : 0;
+    const int nbins = pass == 2 ? 1024 : 2048;
+    for (int i = threadIdx.x; i < nbins; i += kTopkThreads) hist[i] = 0;
+    __syncthreads();
+    if (fits) {
+      for (int c = threadIdx.x; c < nc; c += kTopkThreads) {
+        const uint32_t key = skeys[cand[c]];
+        if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & (nbins - 1)], 1u);
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < nloc; i += kTopkThreads) {
+        const uint32_t key = skeys[i];
+        if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & (nbins - 1)], 1u);
+      }
+    }
+    merge(nbins);
+    select_bin(nbins, remaining);
+    prefix |= sel[0] << shift;
+    pmask |= (uint32_t)(nbins - 1) << shift;
+    remaining -= sel[1];
+    __syncthreads();  // sel and hist are rewritten by the next pass
+  }
+  // ---- per warp range, keys above the k-th key and keys equal to it: the
+  // bin's share from the candidates, or a counting pass over the half
+  if (threadIdx.x < 32) {
+    cgt[threadIdx.x] = 0;
+    ceq[threadIdx.x] = 0;
+  }
+  __syncthreads();
+  if (fits) {
+    for (int c = threadIdx.x; c < nc; c += kTopkThreads) {
+      const uint32_t pos = cand[c], key = skeys[pos];
+      const int ww = (int)(pos / wspan);
+      if (key > prefix) atomicAdd(&cgt[ww], 1u);
+      else if (key == prefix) atomicAdd(&ceq[ww], 1u);
+    }
+  } else {
+    uint32_t cg = 0, ce = 0;
+#pragma unroll 4
+    for (int j = 0; j < S; ++j) {
+      const int64_t i = wb + 32 * j + lane;
+      const uint32_t key = i < nloc ? skeys[i] : 0u;
+      cg += __popc(__ballot_sync(0xFFFFFFFFu, i < nloc && key > prefix && (key >> 21) == bin0));
+      ce += __popc(__ballot_sync(0xFFFFFFFFu, i < nloc && key == prefix));
+    }
+    if (lane == 0) {
+      cgt[warp] = cg;
+      ceq[warp] = ce;
+    }
+  }
+  __syncthreads();
+  // ---- this CTA's totals; CTA 1's output starts after CTA 0's
+  if (warp == 0) {
+    uint32_t tg = gabove[lane] + cgt[lane], te = ceq[lane];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      tg += __shfl_xor_sync(0xFFFFFFFFu, tg, off);
+      te += __shfl_xor_sync(0xFFFFFFFFu, te, off);
+    }
+    if (lane == 0) {
+      tot_ge[0] = tg;
+      tot_ge[1] = te;
+    }
+  }
+  cluster_sync_all();
+  uint32_t base_g = 0, base_e = 0;
+  if (peer == 0) {
+    base_g = ld_dsmem(smem_u32(&tot_ge[0]), 0);
+    base_e = ld_dsmem(smem_u32(&tot_ge[1]), 0);
+  }
+  cluster_sync_all();  // CTA 0's totals are read before it may exit
+  // ---- write: ascending positions above the k-th key and the first
+  // `remaining` equal to it (lim > k: exactly k in all).  This CTA's counts
+  // are below 2^16 (<= 48 K positions), so one packed scan orders the warps.
+  {
+    const uint32_t cg = gabove[warp] + cgt[warp], ce = ceq[warp];
+    uint32_t tot;
+    const uint32_t ex = block_excl_scan(lane == 0 ? ((cg << 16) | ce) : 0u, warp_sums, &tot);
+    const uint32_t exw = __shfl_sync(0xFFFFFFFFu, ex, 0);
+    uint32_t g = base_g + (exw >> 16), e = base_e + (exw & 0xFFFFu);
+#pragma unroll 4
+    for (int j = 0; j < S; ++j) {
+      const int64_t i = wb + 32 * j + lane;
+      const uint32_t key = i < nloc ? skeys[i] : 0u;
+      const bool isg = i < nloc && key > prefix, ise = i < nloc && key == prefix;
+      const uint32_t bg = __ballot_sync(0xFFFFFFFFu, isg), be = __ballot_sync(0xFFFFFFFFu, ise);
+      const uint32_t gb = g + __popc(bg & lt), eb = e + __popc(be & lt);
+      if (isg) o[gb + min(eb, remaining)] = (int32_t)(base + i);
+      else if (ise && eb < remaining) o[gb + eb] = (int32_t)(base + i);
+      g += __popc(bg);
+      e += __popc(be);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kTopkThreads)
     indexer_topk_kernel(const float* logits, int64_t logits_stride, int next_n, const int32_t* ctx,
                         int32_t* out, int64_t out_stride, int k, int64_t max_len) {
-  extern __shared__ uint32_t skeys[];  // kResident: the row's keys
   __shared__ uint32_t hist[2048];
   __shared__ uint32_t warp_sums[32];
   __shared__ uint32_t sel[2];  // chosen bin, keys above it (this pass)
-  __shared__ uint32_t cand[kCand];  // the first pass's chosen-bin keys (resident: positions)
+  __shared__ uint32_t cand[kCand];  // the first pass's chosen-bin keys
   __shared__ uint32_t ncand;
-  __shared__ uint32_t gabove[2][32], cgt[2][32], ceq[2][32];  // per round and warp (resident)
   if (threadIdx.x == 0) pdl_launch_dependents();
   pdl_wait();
   const int64_t r = blockIdx.x;
@@ -390,181 +633,8 @@ __global__ void __launch_bounds__(kTopkThreads)
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t lt = (1u << lane) - 1u;
-  // The bin holding the `remaining`-th largest counted key (bins taken from
-  // the top): thread t owns nbins / 1024 bins and one block scan orders the
-  // threads.  Leaves the bin and the count above it in sel[0], sel[1].
-  auto select_bin = [&](int nbins, uint32_t rem) {
-    const int per = nbins / kTopkThreads;
-    const int hi = nbins - per * (int)threadIdx.x;
-    uint32_t sum = 0;
-    for (int bi = hi - 1; bi >= hi - per; --bi) sum += hist[bi];
-    uint32_t tot;
-    const uint32_t ex = block_excl_scan(sum, warp_sums, &tot);
-    if (ex < rem && ex + sum >= rem) {
-      uint32_t above = ex;
-      int bi = hi - 1;
-      for (; bi > hi - per; --bi) {
-        if (above + hist[bi] >= rem) break;
-        above += hist[bi];
-      }
-      sel[0] = (uint32_t)bi;
-      sel[1] = above;
-    }
-    __syncthreads();
-  };
-  if constexpr (kResident) {
-    // ---- the row into shared memory (16-byte cp.async copies, all of a
-    // thread's in flight at once; unaligned rows and the ragged tail element
-    // by element), converted to keys in place while the first pass's
-    // histogram (top 11 bits) is counted
-    for (int i = threadIdx.x; i < 2048; i += kTopkThreads) hist[i] = 0;
-    __syncthreads();
-    const int64_t n4 = (reinterpret_cast<uintptr_t>(row) & 15u) == 0 ? lim >> 2 : 0;
-    for (int64_t i = threadIdx.x; i < n4; i += kTopkThreads)
-      cp_async16(smem_u32(&skeys[4 * i]), row + 4 * i, 16);
-    cp_async_commit();
-    for (int64_t i = 4 * n4 + threadIdx.x; i < lim; i += kTopkThreads) {
-      const uint32_t key = sortable_key(row[i]);
-      skeys[i] = key;
-      atomicAdd(&hist[key >> 21], 1u);
-    }
-    cp_async_wait<0>();
-    __syncthreads();
-    for (int64_t i = threadIdx.x; i < n4; i += kTopkThreads) {
-      uint4 v = reinterpret_cast<const uint4*>(skeys)[i];
-      v = make_uint4(sortable_key(__uint_as_float(v.x)), sortable_key(__uint_as_float(v.y)),
-                     sortable_key(__uint_as_float(v.z)), sortable_key(__uint_as_float(v.w)));
-      reinterpret_cast<uint4*>(skeys)[i] = v;
-      atomicAdd(&hist[v.x >> 21], 1u);
-      atomicAdd(&hist[v.y >> 21], 1u);
-      atomicAdd(&hist[v.z >> 21], 1u);
-      atomicAdd(&hist[v.w >> 21], 1u);
-    }
-    __syncthreads();
-    uint32_t remaining = (uint32_t)k;
-    select_bin(2048, remaining);
-    const uint32_t bin0 = sel[0];
-    const bool fits = hist[bin0] <= (uint32_t)kCand;  // the bin's keys fit the candidate list
-    uint32_t prefix = bin0 << 21, pmask = 0x7FFu << 21;
-    remaining -= sel[1];
-    // ---- in the write pass's mapping (warp w: positions [1024 w, +1024) of
-    // each 32 K round, lane l position 32 j + l at step j): per warp and
-    // round, the keys above the bin; the bin's positions into the candidates
-    const int rounds = (int)((lim + kRound - 1) / kRound);  // <= 2
-    if (threadIdx.x == 0) ncand = 0;
-    __syncthreads();
-    for (int rd = 0; rd < rounds; ++rd) {
-      const int64_t wb = (int64_t)rd * kRound + (int64_t)warp * 1024;
-      uint32_t ga = 0;
-#pragma unroll 4
-      for (int j = 0; j < 32; ++j) {
-        const int64_t i = wb + 32 * j + lane;
-        const bool v = i < lim;
-        const uint32_t top = v ? skeys[i] >> 21 : 0u;
-        ga += __popc(__ballot_sync(0xFFFFFFFFu, v && top > bin0));
-        if (fits) {
-          const bool m = v && top == bin0;
-          const uint32_t bal = __ballot_sync(0xFFFFFFFFu, m);
-          uint32_t base = 0;
-          if (lane == 0 && bal != 0) base = atomicAdd(&ncand, (uint32_t)__popc(bal));
-          base = __shfl_sync(0xFFFFFFFFu, base, 0);
-          if (m) cand[base + __popc(bal & lt)] = (uint32_t)i;
-        }
-      }
-      if (lane == 0) gabove[rd][warp] = ga;
-    }
-    __syncthreads();
-    // ---- the two refining passes over the bin's keys (or, when they did not
-    // fit, over the whole row)
-    const int nc = fits ? (int)ncand : 0;
-#pragma unroll 1
-    for (int pass = 1; pass < 3; ++pass) {
-      const int shift = pass == 1 ? 10 : 0;
-      const int nbins = pass == 2 ? 1024 : 2048;
-      for (int i = threadIdx.x; i < nbins; i += kTopkThreads) hist[i] = 0;
-      __syncthreads();
-      if (fits) {
-        for (int c = threadIdx.x; c < nc; c += kTopkThreads) {
-          const uint32_t key = skeys[cand[c]];
-          if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & (nbins - 1)], 1u);
-        }
-      } else {
-        for (int64_t i = threadIdx.x; i < lim; i += kTopkThreads) {
-          const uint32_t key = skeys[i];
-          if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & (nbins - 1)], 1u);
-        }
-      }
-      __syncthreads();
-      select_bin(nbins, remaining);
-      prefix |= sel[0] << shift;
-      pmask |= (uint32_t)(nbins - 1) << shift;
-      remaining -= sel[1];
-      __syncthreads();  // sel and hist are rewritten by the next pass
-    }
-    // ---- per warp and round, keys above the k-th key and keys equal to it:
-    // the bin's share from the candidates, or a counting pass over the row
-    if (threadIdx.x < 2 * 32) {
-      cgt[threadIdx.x >> 5][threadIdx.x & 31] = 0;
-      ceq[threadIdx.x >> 5][threadIdx.x & 31] = 0;
-    }
-    __syncthreads();
-    if (fits) {
-      for (int c = threadIdx.x; c < nc; c += kTopkThreads) {
-        const uint32_t pos = cand[c], key = skeys[pos];
-        const int rd = (int)(pos / kRound), ww = (int)((pos % kRound) >> 10);
-        if (key > prefix) atomicAdd(&cgt[rd][ww], 1u);
-        else if (key == prefix) atomicAdd(&ceq[rd][ww], 1u);
-      }
-    } else {
-      for (int rd = 0; rd < rounds; ++rd) {
-        const int64_t wb = (int64_t)rd * kRound + (int64_t)warp * 1024;
-        uint32_t cg = 0, ce = 0;
-#pragma unroll 4
-        for (int j = 0; j < 32; ++j) {
-          const int64_t i = wb + 32 * j + lane;
-          const uint32_t key = i < lim ? skeys[i] : 0u;
-          cg += __popc(__ballot_sync(0xFFFFFFFFu, i < lim && key > prefix && (key >> 21) == bin0));
-          ce += __popc(__ballot_sync(0xFFFFFFFFu, i < lim && key == prefix));
-        }
-        if (lane == 0) {
-          cgt[rd][warp] = cg;
-          ceq[rd][warp] = ce;
-        }
-      }
-    }
-    __syncthreads();
-    // ---- write: ascending positions above the k-th key and the first
-    // `remaining` equal to it, then nothing else (lim > k: exactly k)
-    uint32_t base_g = 0, base_e = 0;
-    for (int rd = 0; rd < rounds; ++rd) {
-      const int64_t wb = (int64_t)rd * kRound + (int64_t)warp * 1024;
-      const uint32_t cg = gabove[rd][warp] + cgt[rd][warp], ce = ceq[rd][warp];
-      uint32_t tot;
-      const uint32_t ex = block_excl_scan(lane == 0 ? ((cg << 16) | ce) : 0u, warp_sums, &tot);
-      const uint32_t exw = __shfl_sync(0xFFFFFFFFu, ex, 0);
-      uint32_t g = base_g + (exw >> 16), e = base_e + (exw & 0xFFFFu);
-#pragma unroll 4
-      for (int j = 0; j < 32; ++j) {
-        const int64_t i = wb + 32 * j + lane;
-        const uint32_t key = i < lim ? skeys[i] : 0u;
-        const bool isg = i < lim && key > prefix, ise = i < lim && key == prefix;
-        const uint32_t bg = __ballot_sync(0xFFFFFFFFu, isg), be = __ballot_sync(0xFFFFFFFFu, ise);
-        const uint32_t gb = g + __popc(bg & lt), eb = e + __popc(be & lt);
-        if (isg) o[gb + min(eb, remaining)] = (int32_t)i;
-        else if (ise && eb < remaining) o[gb + eb] = (int32_t)i;
-        g += __popc(bg);
-        e += __popc(be);
-      }
-      base_g += tot >> 16;
-      base_e += tot & 0xFFFFu;
-    }
-    return;
-  }
-  // ===== rows above the resident limit: every pass reads the row (from L2)
-  auto key_at = [&](int64_t i) -> uint32_t {
-    if constexpr (kResident) return skeys[i];
-    return sortable_key(row[i]);
-  };
+  // every pass reads the row (from L2)
+  auto key_at = [&](int64_t i) -> uint32_t { return sortable_key(row[i]); };
   // radix select of the k-th largest key: 11 + 11 + 10 bits.  After the first
   // pass the keys of the chosen bin (usually a few percent of the row) are
   // compacted, and the later passes count only them; a bin of more than
@@ -728,18 +798,18 @@ int launch_indexer_logits(const uint8_t* q, int64_t B, int64_t next_n, int64_t q
 int launch_indexer_topk(const float* logits, int64_t rows, int64_t logits_stride, int64_t next_n,
                         const int32_t* ctx, int32_t* out, int64_t out_stride, int64_t topk,
                         int64_t max_len, cudaStream_t st) {
-  if (max_len <= idx::kSmemKeys) {
-    const size_t smem = (size_t)max_len * sizeof(uint32_t);
-    cudaError_t e = cudaFuncSetAttribute(idx::indexer_topk_kernel<true>,
+  if (max_len <= idx::kPairMaxLen) {
+    const size_t smem = (size_t)idx::pair_half(max_len) * sizeof(uint32_t);
+    cudaError_t e = cudaFuncSetAttribute(idx::indexer_topk_pair_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)(idx::kSmemKeys * sizeof(uint32_t)));
     if (e != cudaSuccess) return check_cuda(e, "indexer top-k smem attribute");
-    return check_cuda(launch_pdl(idx::indexer_topk_kernel<true>, dim3((unsigned)rows),
+    return check_cuda(launch_pdl(idx::indexer_topk_pair_kernel, dim3((unsigned)(2 * rows)),
                                  dim3(idx::kTopkThreads), smem, st, logits, logits_stride,
                                  (int)next_n, ctx, out, out_stride, (int)topk, max_len),
-                      "indexer_topk_kernel launch");
+                      "indexer_topk_pair_kernel launch");
   }
-  return check_cuda(launch_pdl(idx::indexer_topk_kernel<false>, dim3((unsigned)rows),
+  return check_cuda(launch_pdl(idx::indexer_topk_kernel, dim3((unsigned)rows),
                                dim3(idx::kTopkThreads), 0, st, logits, logits_stride, (int)next_n,
                                ctx, out, out_stride, (int)topk, max_len),
                     "indexer_topk_kernel launch");
