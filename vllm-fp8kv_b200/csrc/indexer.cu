@@ -29,11 +29,13 @@
 // Two accumulator buffers in tensor memory let the epilogue of tile t overlap
 // the MMAs of tile t+1.  Every wait is bounded (status word, as the decode).
 //
-// Top-k kernel: one CTA per logits row.  Logits map to order-preserving
-// 32-bit keys (kept in shared memory for rows of up to 48 K positions); three
-// histogram passes (11, 11 and 10 bits) find the k-th largest key exactly; a
-// final pass in position order writes every position above it and the
-// lowest-positioned ties, ascending, then -1 padding.
+// Top-k: a 2-CTA cluster per logits row (one CTA per row for rows above
+// 96,256 positions).  Logits map to order-preserving 32-bit keys, kept in
+// shared memory (each CTA its half of the row); three histogram passes (11, 11
+// and 10 bits, the two CTAs' counts added through distributed shared memory)
+// find the k-th largest key exactly; a final pass in position order writes
+// every position above it and the lowest-positioned ties, ascending, then -1
+// padding.
 #include "common.cuh"
 #include "decode.h"
 #include "tc_cluster.cuh"
