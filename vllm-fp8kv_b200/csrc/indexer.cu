@@ -54,7 +54,7 @@ constexpr int kHeads = 64;                // index heads per query token
 constexpr int kBlock = 64;                // tokens per cache block
 constexpr int kPageBytes = kBlock * (kDim + 4);   // 8448
 constexpr int kTileTokens = 128;          // MMA M: two blocks
-constexpr int kStages = 5;
+constexpr int kStages = 4;
 constexpr int kStageBytes = kTileTokens * kDim;   // 16 KB of values
 constexpr int kMaxNextN = 2;              // N = 64 * next_n query heads <= 128
 constexpr int kThreads = 6 * 32;
@@ -69,13 +69,13 @@ __host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
 
 struct Smem {
   uint8_t kv[kStages][kStageBytes];        // 1024-aligned: swizzled operand tiles
-  uint8_t q[kMaxNextN * kHeads * kDim];    // 1024-aligned: N rows of 128 B, swizzled
+  uint8_t q[2][kMaxNextN * kHeads * kDim]; // 1024-aligned: N rows of 128 B, swizzled, by item parity
   float scale[kStages][kTileTokens];
-  float w[kMaxNextN * kHeads];
+  float w[2][kMaxNextN * kHeads];          // by item parity
   uint8_t pvalid[kStages][2];              // block p of the stage's tile was loaded
   uint64_t full[kStages], empty[kStages];
   uint64_t tfull[2], tempty[2];
-  uint64_t qready, drain;
+  uint64_t qfull[2], qempty[2], drain;
   uint32_t tmem_base;
 };
 static_assert(offsetof(Smem, q) % 1024 == 0, "swizzle atoms need 1024-B alignment");
@@ -94,7 +94,9 @@ struct Args {
   float* logits;             // [B * next_n, logits_stride]
   int64_t logits_stride, max_len;
   int next_n;
-  int tiles_per_cta;
+  int tiles_per_item;        // tiles of a work item (a chunk of one request's context)
+  int chunks_per_req;        // items per request
+  int items;                 // B * chunks_per_req
 };
 
 // The epilogue warps' own barrier (id 1; the other warps never use it).
@@ -134,132 +136,186 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 namespace {
 
 // ------------------------------------------------------------------ logits
-__device__ void producer(const Args& a, Smem& s, const CUtensorMap* tm, int b, int t0, int ncomp,
-                         int ctx) {
-  int armed = 0;
+// Persistent: CTA x walks items u = x, x + gridDim.x, ...; an item is
+// tiles_per_item tiles of one request's context.  Every role walks the same
+// sequence; the stage ring and the accumulator buffers run across items (i
+// counts the CTA's computed tiles), the query rows and head weights are
+// double-buffered by item parity (k counts the CTA's items).
+struct Item {
+  int b, t0, ntiles, ncomp, ctx;
+};
+__device__ __forceinline__ Item item_of(const Args& a, int u) {
+  Item it;
+  it.b = u / a.chunks_per_req;
+  it.t0 = (u % a.chunks_per_req) * a.tiles_per_item;
+  const int total_tiles = (int)((a.max_len + kTileTokens - 1) / kTileTokens);
+  it.ntiles = max(0, min(a.tiles_per_item, total_tiles - it.t0));
+  it.ctx = max(0, a.ctx[it.b]);
+  // tiles with a token below the context are computed; the rest are -inf
+  const int ctx_tiles = (int)(((int64_t)it.ctx + kTileTokens - 1) / kTileTokens);
+  it.ncomp = max(0, min(it.ntiles, ctx_tiles - it.t0));
+  return it;
+}
+
+__device__ void producer(const Args& a, Smem& s, const CUtensorMap* tm) {
+  int i = 0;
   bool ok = true;
-  for (int i = 0; i < ncomp; ++i) {
-    const int st = i % kStages, t = t0 + i;
-    if (i >= kStages) ok = thread_wait(smem_u32(&s.empty[st]), ((i / kStages) + 1) & 1, 50);
-    if (!ok) break;
-    int32_t bid[2];
-    uint32_t bytes = 0;
+  for (int u = blockIdx.x; u < a.items && ok; u += gridDim.x) {
+    const Item it = item_of(a, u);
+    for (int ii = 0; ii < it.ncomp; ++ii, ++i) {
+      const int st = i % kStages, t = it.t0 + ii;
+      if (i >= kStages) ok = thread_wait(smem_u32(&s.empty[st]), ((i / kStages) + 1) & 1, 50);
+      if (!ok) break;
+      int32_t bid[2];
+      uint32_t bytes = 0;
 #pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      const int64_t pos = 2 * (int64_t)t + p;  // block of the request
-      bid[p] = -1;
-      if ((int64_t)t * kTileTokens + p * kBlock < ctx && pos < a.max_blocks) {
-        const int32_t v = a.bt[(int64_t)b * a.bt_stride + pos];
-        if (v >= 0 && v < a.num_blocks) bid[p] = v;
+      for (int p = 0; p < 2; ++p) {
+        const int64_t pos = 2 * (int64_t)t + p;  // block of the request
+        bid[p] = -1;
+        if ((int64_t)t * kTileTokens + p * kBlock < it.ctx && pos < a.max_blocks) {
+          const int32_t v = a.bt[(int64_t)it.b * a.bt_stride + pos];
+          if (v >= 0 && v < a.num_blocks) bid[p] = v;
+        }
+        s.pvalid[st][p] = bid[p] >= 0 ? 1 : 0;
+        if (bid[p] >= 0) bytes += kBlock * kDim + kBlock * 4;
       }
-      s.pvalid[st][p] = bid[p] >= 0 ? 1 : 0;
-      if (bid[p] >= 0) bytes += kBlock * kDim + kBlock * 4;
-    }
-    const uint32_t bar = smem_u32(&s.full[st]);
-    mbar_arrive_expect_tx(bar, bytes);  // releases the flags above
+      const uint32_t bar = smem_u32(&s.full[st]);
+      mbar_arrive_expect_tx(bar, bytes);  // releases the flags above
 #pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      if (bid[p] < 0) continue;
-      tma_load_page(smem_u32(s.kv[st]) + p * kBlock * kDim, tm, bid[p], bar);
-      bulk_g2s(smem_u32(&s.scale[st][p * kBlock]),
-               a.k_cache + (int64_t)bid[p] * kPageBytes + kBlock * kDim, kBlock * 4, bar);
+      for (int p = 0; p < 2; ++p) {
+        if (bid[p] < 0) continue;
+        tma_load_page(smem_u32(s.kv[st]) + p * kBlock * kDim, tm, bid[p], bar);
+        bulk_g2s(smem_u32(&s.scale[st][p * kBlock]),
+                 a.k_cache + (int64_t)bid[p] * kPageBytes + kBlock * kDim, kBlock * 4, bar);
+      }
     }
-    ++armed;
   }
   // no copy may outlive the CTA: the stages armed last have landed (full limit)
-  for (int x = armed > kStages ? armed - kStages : 0; x < armed; ++x)
+  for (int x = i > kStages ? i - kStages : 0; x < i; ++x)
     (void)thread_wait(smem_u32(&s.full[x % kStages]), (x / kStages) & 1, 51);
 }
 
-__device__ void mma_issuer(const Args& a, Smem& s, uint32_t tmem, int ncomp, int N) {
-  bool ok = thread_wait(smem_u32(&s.qready), 0, 52);
-  tc_fence_after();
-  const uint64_t qdesc = sdesc_sw128(smem_u32(s.q), 16, 1024);
+__device__ void mma_issuer(const Args& a, Smem& s, uint32_t tmem, int N) {
   const uint32_t idesc = idesc_e4m3(kTileTokens, N);
-  for (int i = 0; i < ncomp && ok; ++i) {
-    const int st = i % kStages, buf = i & 1;
-    ok = thread_wait(smem_u32(&s.full[st]), (i / kStages) & 1, 53);
-    if (ok && i >= 2) ok = thread_wait(smem_u32(&s.tempty[buf]), ((i >> 1) + 1) & 1, 54);
+  int i = 0, k = 0;
+  bool ok = true;
+  for (int u = blockIdx.x; u < a.items && ok; u += gridDim.x, ++k) {
+    const int ncomp = item_of(a, u).ncomp;
+    const int qb = k & 1;
+    ok = thread_wait(smem_u32(&s.qfull[qb]), (k >> 1) & 1, 52);
     if (!ok) break;
     tc_fence_after();
-    const uint64_t adesc = sdesc_sw128(smem_u32(s.kv[st]), 16, 1024);
+    const uint64_t qdesc = sdesc_sw128(smem_u32(s.q[qb]), 16, 1024);
+    for (int ii = 0; ii < ncomp && ok; ++ii, ++i) {
+      const int st = i % kStages, buf = i & 1;
+      ok = thread_wait(smem_u32(&s.full[st]), (i / kStages) & 1, 53);
+      if (ok && i >= 2) ok = thread_wait(smem_u32(&s.tempty[buf]), ((i >> 1) + 1) & 1, 54);
+      if (!ok) break;
+      tc_fence_after();
+      const uint64_t adesc = sdesc_sw128(smem_u32(s.kv[st]), 16, 1024);
 #pragma unroll
-    for (int k = 0; k < kDim / 32; ++k)  // 32 e4m3 values = 32 bytes per k-step
-      mma_f8(tmem + buf * N, adesc + (uint64_t)((k * 32) >> 4), qdesc + (uint64_t)((k * 32) >> 4),
-             idesc, k > 0 ? 1u : 0u);
-    mma_commit(smem_u32(&s.empty[st]));
-    mma_commit(smem_u32(&s.tfull[buf]));
+      for (int kk = 0; kk < kDim / 32; ++kk)  // 32 e4m3 values = 32 bytes per k-step
+        mma_f8(tmem + buf * N, adesc + (uint64_t)((kk * 32) >> 4), qdesc + (uint64_t)((kk * 32) >> 4),
+               idesc, kk > 0 ? 1u : 0u);
+      mma_commit(smem_u32(&s.empty[st]));
+      mma_commit(smem_u32(&s.tfull[buf]));
+    }
+    // this item's query buffer is free once its MMAs complete (at once when
+    // it had none)
+    mma_commit(smem_u32(&s.qempty[qb]));
   }
   // drain: no MMA may still run when tensor memory is freed
   mma_commit(smem_u32(&s.drain));
   (void)thread_wait(smem_u32(&s.drain), 0, 55);
 }
 
-__device__ void epilogue(const Args& a, Smem& s, uint32_t tmem, int b, int t0, int ntiles,
-                         int ncomp, int ctx, int N) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = threadIdx.x;  // TMEM lane = token of the tile
+// The request's query rows (swizzled K-major operand) and head weights into
+// buffer qb; announced on qfull[qb] after every epilogue warp's stores.
+__device__ void load_query(const Args& a, Smem& s, int b, int qb, int N, int lane) {
   const int nn = a.next_n;
-  // the request's query rows (swizzled K-major operand) and head weights
   const uint4* qsrc = reinterpret_cast<const uint4*>(a.q + (int64_t)b * a.q_stride_b);
   for (int c = threadIdx.x; c < N * (kDim / 16); c += 128) {
     const int row = c >> 3, chunk = c & 7;
-    *reinterpret_cast<uint4*>(s.q + swz128(row, chunk)) = qsrc[c];
+    *reinterpret_cast<uint4*>(s.q[qb] + swz128(row, chunk)) = qsrc[c];
   }
   for (int c = threadIdx.x; c < N; c += 128)
-    s.w[c] = a.w[((int64_t)b * nn + c / kHeads) * a.w_stride + (c % kHeads)];
+    s.w[qb][c] = a.w[((int64_t)b * nn + c / kHeads) * a.w_stride + (c % kHeads)];
   fence_proxy_async_smem();
   __syncwarp();
-  if (lane == 0) mbar_arrive(smem_u32(&s.qready));
-  named_sync_epi();  // s.w is read by every epilogue thread below
+  if (lane == 0) mbar_arrive(smem_u32(&s.qfull[qb]));
+}
+
+__device__ void epilogue(const Args& a, Smem& s, uint32_t tmem, int N) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = threadIdx.x;  // TMEM lane = token of the tile
+  const int nn = a.next_n;
   const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
   bool ok = true;
-  for (int i = 0; i < ntiles; ++i) {
-    const int64_t tok = (int64_t)(t0 + i) * kTileTokens + r;
-    float v[kMaxNextN];
+  int i = 0, k = 0;
+  if ((int)blockIdx.x < a.items) load_query(a, s, item_of(a, blockIdx.x).b, 0, N, lane);
+  for (int u = blockIdx.x; u < a.items; u += gridDim.x, ++k) {
+    const Item it = item_of(a, u);
+    // the next item's query rows and weights into the other buffer, once the
+    // MMAs of the item before this one (its last user) are complete and every
+    // epilogue warp has finished that item's tiles (its weights)
+    const int un = u + gridDim.x;
+    named_sync_epi();
+    if (un < a.items) {
+      if (k >= 1 && ok) ok = warp_wait(smem_u32(&s.qempty[(k + 1) & 1]), ((k - 1) >> 1) & 1, 58);
+      load_query(a, s, item_of(a, un).b, (k + 1) & 1, N, lane);
+    }
+    // every epilogue warp reaches these barriers twice per item whatever `ok`
+    // is (a warp whose wait gave up keeps walking the items without work)
+    named_sync_epi();  // s.w[k & 1] (stored one item ago) is read below
+    const float* wk = s.w[k & 1];
+    for (int ii = 0; ii < it.ntiles; ++ii) {
+      const int64_t tok = (int64_t)(it.t0 + ii) * kTileTokens + r;
+      float v[kMaxNextN];
 #pragma unroll
-    for (int n = 0; n < kMaxNextN; ++n) v[n] = -INFINITY;
-    if (i < ncomp && ok) {
-      const int st = i % kStages, buf = i & 1;
-      ok = warp_wait(smem_u32(&s.tfull[buf]), (i >> 1) & 1, 56);
-      if (ok) ok = warp_wait(smem_u32(&s.full[st]), (i / kStages) & 1, 57);
-      if (ok) {
-        (void)mbar_try_wait(smem_u32(&s.full[st]), (i / kStages) & 1);  // every lane acquires
-        tc_fence_after();
-        float acc[kMaxNextN];
+      for (int n = 0; n < kMaxNextN; ++n) v[n] = -INFINITY;
+      if (ii < it.ncomp) {
+        const int st = i % kStages, buf = i & 1;
+        ++i;
+        if (ok) ok = warp_wait(smem_u32(&s.tfull[buf]), ((i - 1) >> 1) & 1, 56);
+        if (ok) ok = warp_wait(smem_u32(&s.full[st]), ((i - 1) / kStages) & 1, 57);
+        if (ok) {
+          (void)mbar_try_wait(smem_u32(&s.full[st]), ((i - 1) / kStages) & 1);  // every lane acquires
+          tc_fence_after();
+          float acc[kMaxNextN];
 #pragma unroll
-        for (int n = 0; n < kMaxNextN; ++n) {
-          acc[n] = 0.f;
-          if (n < nn) {
-            uint32_t d0[32], d1[32];
-            tmem_ld32(trow + buf * N + n * kHeads, d0);
-            tmem_ld32(trow + buf * N + n * kHeads + 32, d1);
-            tmem_wait_ld();
-            const float* w = s.w + n * kHeads;
+          for (int n = 0; n < kMaxNextN; ++n) {
+            acc[n] = 0.f;
+            if (n < nn) {
+              uint32_t d0[32], d1[32];
+              tmem_ld32(trow + buf * N + n * kHeads, d0);
+              tmem_ld32(trow + buf * N + n * kHeads + 32, d1);
+              tmem_wait_ld();
+              const float* w = wk + n * kHeads;
 #pragma unroll
-            for (int h = 0; h < 32; ++h) {
-              acc[n] = fmaf(fmaxf(__uint_as_float(d0[h]), 0.f), w[h], acc[n]);
-              acc[n] = fmaf(fmaxf(__uint_as_float(d1[h]), 0.f), w[32 + h], acc[n]);
+              for (int h = 0; h < 32; ++h) {
+                acc[n] = fmaf(fmaxf(__uint_as_float(d0[h]), 0.f), w[h], acc[n]);
+                acc[n] = fmaf(fmaxf(__uint_as_float(d1[h]), 0.f), w[32 + h], acc[n]);
+              }
             }
           }
+          const float sc = s.scale[st][r];
+          const bool live = s.pvalid[st][r >> 6] != 0;
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(smem_u32(&s.tempty[buf]));  // accumulator buffer read
+            mbar_arrive(smem_u32(&s.empty[st]));    // scales and flags read
+          }
+#pragma unroll
+          for (int n = 0; n < kMaxNextN; ++n)
+            if (n < nn && live && tok < (int64_t)it.ctx - nn + n + 1) v[n] = acc[n] * sc;
         }
-        const float sc = s.scale[st][r];
-        const bool live = s.pvalid[st][r >> 6] != 0;
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(smem_u32(&s.tempty[buf]));  // accumulator buffer read
-          mbar_arrive(smem_u32(&s.empty[st]));    // scales and flags read
-        }
+      }
+      if (tok < a.max_len) {
 #pragma unroll
         for (int n = 0; n < kMaxNextN; ++n)
-          if (n < nn && live && tok < (int64_t)ctx - nn + n + 1) v[n] = acc[n] * sc;
+          if (n < nn) a.logits[((int64_t)it.b * nn + n) * a.logits_stride + tok] = v[n];
       }
-    }
-    if (tok < a.max_len) {
-#pragma unroll
-      for (int n = 0; n < kMaxNextN; ++n)
-        if (n < nn) a.logits[((int64_t)b * nn + n) * a.logits_stride + tok] = v[n];
     }
   }
 }
@@ -273,12 +329,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t pad = ((raw_base + 1023u) & ~1023u) - raw_base;
   Smem& s = *reinterpret_cast<Smem*>(smem_raw + pad);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.y;
   const int N = kHeads * a.next_n;
   const uint32_t tmem_cols = N <= 64 ? 128u : 256u;  // two accumulator buffers
-  const int total_tiles = (int)((a.max_len + kTileTokens - 1) / kTileTokens);
-  const int t0 = blockIdx.x * a.tiles_per_cta;
-  const int ntiles = max(0, min(a.tiles_per_cta, total_tiles - t0));
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -288,8 +340,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&s.tfull[i]), 1);
       mbar_init(smem_u32(&s.tempty[i]), 4);
+      mbar_init(smem_u32(&s.qfull[i]), 4);
+      mbar_init(smem_u32(&s.qempty[i]), 1);
     }
-    mbar_init(smem_u32(&s.qready), 4);
     mbar_init(smem_u32(&s.drain), 1);
     mbar_init_fence();
   }
@@ -303,18 +356,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) pdl_launch_dependents();
   pdl_wait();  // the previous kernel of the stream has completed: global memory from here on
   const uint32_t tmem = s.tmem_base;
-  const int ctx = max(0, a.ctx[b]);
-  // tiles with a token below the context are computed; the rest are -inf
-  const int ctx_tiles = (int)(((int64_t)ctx + kTileTokens - 1) / kTileTokens);
-  const int ncomp = max(0, min(ntiles, ctx_tiles - t0));
 
   if (warp < 4) {
-    epilogue(a, s, tmem, b, t0, ntiles, ncomp, ctx, N);
+    epilogue(a, s, tmem, N);
   } else if (warp == kProducerWarp) {
-    if (lane == 0) producer(a, s, &tm, b, t0, ncomp, ctx);
+    if (lane == 0) producer(a, s, &tm);
     __syncwarp();
   } else {
-    if (lane == 0) mma_issuer(a, s, tmem, ncomp, N);
+    if (lane == 0) mma_issuer(a, s, tmem, N);
     __syncwarp();
   }
   tc_fence_before();
@@ -782,17 +831,23 @@ int launch_indexer_logits(const uint8_t* q, int64_t B, int64_t next_n, int64_t q
   a.logits_stride = logits_stride;
   a.max_len = max_len;
   a.next_n = (int)next_n;
-  // chunks of up to 16 tiles (2048 tokens); smaller chunks when the batch would
-  // leave SMs idle (two CTAs fit an SM)
+  // items of 8 tiles (1024 tokens), fewer when the batch would leave CTA
+  // slots idle (two CTAs fit an SM); a persistent grid of at most two CTAs per
+  // SM walks them
   const int64_t total_tiles = (max_len + idx::kTileTokens - 1) / idx::kTileTokens;
-  int64_t tpc = 16;
-  while (tpc > 2 && B * ((total_tiles + tpc - 1) / tpc) < 2 * (int64_t)sms) tpc >>= 1;
-  a.tiles_per_cta = (int)tpc;
+  int64_t tpi = 8;
+  while (tpi > 2 && B * ((total_tiles + tpi - 1) / tpi) < 2 * (int64_t)sms) tpi >>= 1;
+  a.tiles_per_item = (int)tpi;
+  a.chunks_per_req = (int)((total_tiles + tpi - 1) / tpi);
+  const int64_t items = B * (int64_t)a.chunks_per_req;
+  if (items > INT32_MAX) return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "too many indexer work items");
+  a.items = (int)items;
+  if (a.items == 0) return FP8MLA_OK;
   const size_t smem = sizeof(idx::Smem) + 1024;
   cudaError_t e = cudaFuncSetAttribute(idx::indexer_logits_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "indexer logits smem attribute");
-  const dim3 grid((unsigned)((total_tiles + tpc - 1) / tpc), (unsigned)B);
+  const dim3 grid((unsigned)std::min<int64_t>(items, 2 * (int64_t)sms));
   return check_cuda(launch_pdl(idx::indexer_logits_kernel, grid, dim3(idx::kThreads), smem, st, a, tm),
                     "indexer_logits_kernel launch");
 }
