@@ -1,7 +1,7 @@
 """Benchmark: fp8 sparse-MLA decode on B200, B=64, H=128, top-k=2048 per GPU.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c2|c3|c4|c5]
+                    [--workload c2|c3|c4|c5|idx|writer]
 
 One step = one decode call over one batch (64 requests x 128 heads x 2048
 selected 656-byte rows).  Multi-GPU: one process per GPU (torchrun), requests
@@ -534,14 +534,124 @@ def run_indexer(args):
     }
 
 
+def run_writer(args):
+    """The fp8_ds_mla cache writer (concat_and_cache_mla(..., "fp8_ds_mla")) on a
+    65,536-token prefill chunk: bf16 latent + rope -> 656-byte rows at random
+    distinct slots of the c2-sized pool (2,097,152 slots).  One step = one
+    writer call; four rotating input sets (302 MB > L2).  Algorithmic bytes
+    per token: 1152 read + 656 written + 8 of slot mapping."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle as O
+    from vllm_fp8kv.cache_writer import concat_and_cache_mla
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    N, slots = 65536, 2_097_152
+    g = torch.Generator(device=dev).manual_seed(11)
+    cache = torch.zeros((slots // 64, 64, 656), dtype=torch.uint8, device=dev)
+    sets = []
+    for _ in range(N_SETS):
+        kv_c = torch.randn((N, 512), generator=g, device=dev).bfloat16()
+        k_pe = torch.randn((N, 64), generator=g, device=dev).bfloat16()
+        sm = torch.randperm(slots, generator=g, device=dev)[:N].to(torch.int64)
+        sets.append((kv_c, k_pe, sm))
+    one = torch.ones((), dtype=torch.float32, device=dev)
+
+    def step(i):
+        kv_c, k_pe, sm = sets[i % N_SETS]
+        concat_and_cache_mla(kv_c, k_pe, cache, sm, "fp8_ds_mla", one)
+
+    stream = torch.cuda.current_stream(dev)
+    clk = ClockSampler(0)
+    clk.__enter__()
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+
+    # end to end: each step's inputs from pinned host memory, one written row back
+    host = [(kv_c.cpu().pin_memory(), k_pe.cpu().pin_memory(), sm.cpu().pin_memory())
+            for kv_c, k_pe, sm in sets]
+    dkv = torch.empty_like(sets[0][0]); dpe = torch.empty_like(sets[0][1]); dsm = torch.empty_like(sets[0][2])
+    row_back = torch.empty((656,), dtype=torch.uint8).pin_memory()
+
+    def e2e_step(i):
+        hkv, hpe, hsm = host[i % N_SETS]
+        dkv.copy_(hkv, non_blocking=True)
+        dpe.copy_(hpe, non_blocking=True)
+        dsm.copy_(hsm, non_blocking=True)
+        concat_and_cache_mla(dkv, dpe, cache, dsm, "fp8_ds_mla", one)
+        row_back.copy_(cache.view(-1, 656)[hsm[0].item()], non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize(dev)
+    e_steps = max(3, args.steps // 20)
+    e0.record(stream)
+    for i in range(e_steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clk.__exit__(None, None, None)
+    e2e_ms = e0.elapsed_time(e1) / e_steps
+
+    bytes_step = N * (1152 + 656 + 8)
+    peaks = _peaks()
+    achieved = bytes_step / (ms * 1e-3) / 1e9
+    roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"] + " (burst)",
+            "kernel": "ds_mla_write_kernel", "time_source": "back-to-back window = ms_per_step",
+            "kernel_us": ms * 1e3, "traffic": _traffic_per_launch("ds_mla_write_kernel", "writer"),
+            "algorithmic_bytes_per_launch": bytes_step}
+    line = {
+        "metric": "fp8_ds_mla cache write GB/s (bf16 latent + rope -> 656-B rows)",
+        "value": achieved, "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "us_per_call": ms * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 -> e4m3", "data": "synthetic",
+        "config": {"workload": f"writer: N={N} tokens, pool={slots} slots, random distinct slots",
+                   "l2": f"{N_SETS} rotating input sets, {N_SETS * N * 1152 / 1e6:.0f} MB > 126 MB L2"},
+        "roofline": roof,
+        "e2e": {"value": bytes_step / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "us_per_call": e2e_ms * 1e3,
+                "h2d_bytes_per_step": N * (1152 + 8), "d2h_bytes_per_step": 656},
+        "gpu_launches": args.steps, "clocks": clk.summary(),
+    }
+    if not args.no_cpu_baseline:
+        # the oracle writer (C restatement of the reference's writer) on a sample
+        n = 8192
+        src = (np.random.default_rng(0).standard_normal((n, 576)).astype(np.float32)
+               .view(np.uint32) >> 16).astype(np.uint16)
+        O.quantize_rows(src)
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            O.quantize_rows(src)
+            reps += 1
+            if time.perf_counter() - t0 > 3.0:
+                break
+        dt = (time.perf_counter() - t0) / reps
+        line["cpu_baseline"] = {"value": n * (1152 + 656 + 8) / dt / 1e9, "unit": "GB/s", "cores": 1,
+                                "kind": "port",
+                                "sample": f"{n} tokens through the oracle's C writer, {reps} timed calls"}
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5", "idx"],
-                    help="c2-c5: the decode shapes; idx: the DSA indexer read path (one GPU)")
+    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5", "idx", "writer"],
+                    help="c2-c5: the decode shapes; idx: the DSA indexer read path; writer: the "
+                         "fp8_ds_mla cache writer (one GPU)")
     ap.add_argument("--requests", type=int, default=0,
                     help="per-GPU batch override for profiling a smaller case (0 = the workload's)")
     ap.add_argument("--cpu-sample", type=int, default=8,
@@ -559,9 +669,9 @@ def main():
             print(json.dumps(line), flush=True)
         return
 
-    if args.workload == "idx":
+    if args.workload in ("idx", "writer"):
         if rank == 0:
-            print(json.dumps(run_indexer(args)), flush=True)
+            print(json.dumps(run_indexer(args) if args.workload == "idx" else run_writer(args)), flush=True)
         return
     line = run_ours(args, rank, world, local_rank)
     if rank == 0 and line is not None:

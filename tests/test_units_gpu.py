@@ -161,6 +161,43 @@ def test_writer_strided_inputs(cuda_device):
     assert np.array_equal(cache.view(-1, 656).cpu().numpy(), want)
 
 
+def test_writer_byte_exact_on_special_values_and_large_random(cuda_device):
+    """Tiles holding +-inf, +-NaN, values near the bf16 maximum, subnormals and
+    signed zeros, then 16,384 tokens of mixed magnitudes: every byte equals the
+    oracle writer, which follows torch's cast, except the sign of a NaN code
+    (0x7F / 0xFF).  inf/inf and NaN propagation give a negative NaN on the
+    host and the canonical positive one on the GPU, so, as the reference's
+    tests do (tests/test_fp8_dequant.py:19-27), NaN codes are compared for
+    NaN-ness only."""
+    rng = np.random.default_rng(4)
+    n = 16384
+    x = rng.standard_normal((n, 576)).astype(np.float32)
+    tile_scale = np.exp(rng.uniform(-20, 20, size=(n, 4))).astype(np.float32)
+    x[:, :512] *= np.repeat(tile_scale, 128, axis=1)
+    specials = [np.inf, -np.inf, np.nan, -np.nan, 3.3e38, -3.3e38, 1e-40, -1e-40, 0.0, -0.0, 1e-38]
+    for r, v in enumerate(specials):
+        x[r, 5 + 128 * (r % 4)] = v
+    x[20, 0:128] = 0.0
+    x[21, 128:256] = -0.0
+    x[22, 256:384] = 1e-39  # a tile whose scale clamps to FLT_MIN
+    src = synthetic.bf16_bits(x)
+    t = U.bf16_tensor(src)
+    cache = torch.zeros(n // 64, 64, 656, dtype=torch.uint8, device="cuda")
+    slots = rng.permutation(n).astype(np.int64)
+    concat_and_cache_ds_mla(t[:, :512].contiguous(), t[:, 512:].contiguous(), cache,
+                            torch.from_numpy(slots).cuda())
+    want = np.zeros((n, 656), np.uint8)
+    O.ds_mla_write(src[:, :512], src[:, 512:], slots, want)
+    got = cache.view(-1, 656).cpu().numpy()
+    latent = np.zeros((656,), bool)
+    latent[:512] = True  # e4m3 codes; scales and rope compare byte for byte
+    nan_code = lambda b: (b & 0x7F) == 0x7F
+    same = (got == want) | (latent & nan_code(want) & nan_code(got))
+    diff = np.argwhere(~same)
+    assert diff.size == 0, f"{len(diff)} bytes differ, first at {diff[:4].tolist()}"
+    assert np.array_equal(nan_code(got) & latent, nan_code(want) & latent)
+
+
 @pytest.mark.parametrize("which", ["in_range", "oob"])
 def test_index_converter_matches_vllm(cuda_device, which):
     g = golden("index.npz")

@@ -124,6 +124,18 @@ __device__ __forceinline__ uint32_t f32_to_e4m3(float x) {
   return r | sign;
 }
 
+// Two values x0 (low byte), x1 (high byte) -> e4m3fn with the hardware's
+// round-to-nearest-even conversion.  Its saturation (to +-448) differs from
+// f32_to_e4m3 (0x7F from 464 up) only for |x| >= 464 and it does not keep NaN
+// signs; the writer uses it only on tiles with a finite scale (no NaN or inf
+// in the tile), where |x / scale| <= 448 * (1 + 2^-24) because
+// scale = RN(amax / 448) (or FLT_MIN, larger).
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float x0, float x1) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;\n" : "=h"(r) : "f"(x1), "f"(x0));
+  return r;
+}
+
 // One warp per token: lane l owns latent elements [16l, 16l+16) (tile l/8),
 // reduces amax over its tile with 8-lane shuffles, divides, converts, and
 // writes 16 bytes; lanes 0..3 write the 4 scales, lanes 0..7 copy the rope.
@@ -172,23 +184,36 @@ __global__ void __launch_bounds__(256) ds_mla_write_kernel(
     float scale = nan ? __uint_as_float(0x7FC00000u) : __fdiv_rn(amax, 448.0f);
     if (!nan && scale < 1.1754944e-38f) scale = 1.1754944e-38f;
     uint32_t q[4];
+    if (scale < INFINITY) {  // finite: no NaN or inf in the tile
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint32_t b0 = f32_to_e4m3(__fdiv_rn(x[4 * j + 0], scale));
-      uint32_t b1 = f32_to_e4m3(__fdiv_rn(x[4 * j + 1], scale));
-      uint32_t b2 = f32_to_e4m3(__fdiv_rn(x[4 * j + 2], scale));
-      uint32_t b3 = f32_to_e4m3(__fdiv_rn(x[4 * j + 3], scale));
-      q[j] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+      for (int j = 0; j < 4; ++j)
+        q[j] = f32x2_to_e4m3x2(__fdiv_rn(x[4 * j + 0], scale), __fdiv_rn(x[4 * j + 1], scale)) |
+               (f32x2_to_e4m3x2(__fdiv_rn(x[4 * j + 2], scale), __fdiv_rn(x[4 * j + 3], scale)) << 16);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t b0 = f32_to_e4m3(__fdiv_rn(x[4 * j + 0], scale));
+        uint32_t b1 = f32_to_e4m3(__fdiv_rn(x[4 * j + 1], scale));
+        uint32_t b2 = f32_to_e4m3(__fdiv_rn(x[4 * j + 2], scale));
+        uint32_t b3 = f32_to_e4m3(__fdiv_rn(x[4 * j + 3], scale));
+        q[j] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+      }
     }
     uint8_t* row = cache + slot * (int64_t)kRowBytes;
     reinterpret_cast<uint4*>(row)[lane] = make_uint4(q[0], q[1], q[2], q[3]);
     if ((lane & 7) == 0) reinterpret_cast<float*>(row + kScaleOff)[lane >> 3] = scale;
     if (lane < 8) {
       const uint16_t* r = k_pe + tok * k_pe_stride + lane * 8;
-      uint32_t p[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) p[j] = (uint32_t)r[2 * j] | ((uint32_t)r[2 * j + 1] << 16);
-      reinterpret_cast<uint4*>(row + kRopeOff)[lane] = make_uint4(p[0], p[1], p[2], p[3]);
+      uint4 p;
+      if ((k_pe_stride % 8) == 0 && (reinterpret_cast<uintptr_t>(k_pe) & 15) == 0) {
+        p = *reinterpret_cast<const uint4*>(r);
+      } else {
+        p.x = (uint32_t)r[0] | ((uint32_t)r[1] << 16);
+        p.y = (uint32_t)r[2] | ((uint32_t)r[3] << 16);
+        p.z = (uint32_t)r[4] | ((uint32_t)r[5] << 16);
+        p.w = (uint32_t)r[6] | ((uint32_t)r[7] << 16);
+      }
+      reinterpret_cast<uint4*>(row + kRopeOff)[lane] = p;
     }
   }
 }
