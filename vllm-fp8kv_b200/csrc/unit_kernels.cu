@@ -139,82 +139,103 @@ __device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float x0, float x1) {
 // One warp per token: lane l owns latent elements [16l, 16l+16) (tile l/8),
 // reduces amax over its tile with 8-lane shuffles, divides, converts, and
 // writes 16 bytes; lanes 0..3 write the 4 scales, lanes 0..7 copy the rope.
+// A warp's next token is loaded before the current one is converted.
 // Reference semantics: tests/fakes.py:28-57, verify/reference.py:68-91.
+struct WriterIn {
+  int64_t slot;
+  uint32_t w[8];  // 16 bf16 latent values
+  uint4 rope;     // lanes 0..7: 8 bf16 rope values
+};
+__device__ __forceinline__ void writer_load(WriterIn& in, const uint16_t* __restrict__ kv_c,
+                                            int64_t kv_c_stride, const uint16_t* __restrict__ k_pe,
+                                            int64_t k_pe_stride, const int64_t* __restrict__ slot_mapping,
+                                            int64_t tok, int lane, bool vec_c, bool vec_pe) {
+  in.slot = slot_mapping[tok];
+  const uint16_t* src = kv_c + tok * kv_c_stride + lane * 16;
+  if (vec_c) {
+    const uint4 a = reinterpret_cast<const uint4*>(src)[0];
+    const uint4 b = reinterpret_cast<const uint4*>(src)[1];
+    in.w[0] = a.x; in.w[1] = a.y; in.w[2] = a.z; in.w[3] = a.w;
+    in.w[4] = b.x; in.w[5] = b.y; in.w[6] = b.z; in.w[7] = b.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) in.w[j] = (uint32_t)src[2 * j] | ((uint32_t)src[2 * j + 1] << 16);
+  }
+  in.rope = make_uint4(0, 0, 0, 0);
+  if (lane < 8) {
+    const uint16_t* r = k_pe + tok * k_pe_stride + lane * 8;
+    if (vec_pe) {
+      in.rope = *reinterpret_cast<const uint4*>(r);
+    } else {
+      in.rope.x = (uint32_t)r[0] | ((uint32_t)r[1] << 16);
+      in.rope.y = (uint32_t)r[2] | ((uint32_t)r[3] << 16);
+      in.rope.z = (uint32_t)r[4] | ((uint32_t)r[5] << 16);
+      in.rope.w = (uint32_t)r[6] | ((uint32_t)r[7] << 16);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256) ds_mla_write_kernel(
     const uint16_t* __restrict__ kv_c, int64_t kv_c_stride, const uint16_t* __restrict__ k_pe,
     int64_t k_pe_stride, const int64_t* __restrict__ slot_mapping, int64_t N,
     uint8_t* __restrict__ cache, int64_t num_slots) {
   const int lane = threadIdx.x & 31;
   const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x / 32);
-  for (int64_t tok = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; tok < N;
-       tok += warps_total) {
-    const int64_t slot = slot_mapping[tok];
-    if (slot < 0 || slot >= num_slots) continue;  // padding token
-    const uint16_t* src = kv_c + tok * kv_c_stride + lane * 16;
-    uint32_t w[8];
-    if ((kv_c_stride % 8) == 0 && (reinterpret_cast<uintptr_t>(kv_c) & 15) == 0) {
-      uint4 a = reinterpret_cast<const uint4*>(src)[0];
-      uint4 b = reinterpret_cast<const uint4*>(src)[1];
-      w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
-      w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
-    } else {
+  const bool vec_c = (kv_c_stride % 8) == 0 && (reinterpret_cast<uintptr_t>(kv_c) & 15) == 0;
+  const bool vec_pe = (k_pe_stride % 8) == 0 && (reinterpret_cast<uintptr_t>(k_pe) & 15) == 0;
+  int64_t tok = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  WriterIn cur, nxt;
+  if (tok < N) writer_load(cur, kv_c, kv_c_stride, k_pe, k_pe_stride, slot_mapping, tok, lane, vec_c, vec_pe);
+  for (; tok < N; tok += warps_total) {
+    if (tok + warps_total < N)
+      writer_load(nxt, kv_c, kv_c_stride, k_pe, k_pe_stride, slot_mapping, tok + warps_total, lane,
+                  vec_c, vec_pe);
+    const int64_t slot = cur.slot;
+    if (slot >= 0 && slot < num_slots) {  // else a padding token
+      float x[16];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) w[j] = (uint32_t)src[2 * j] | ((uint32_t)src[2 * j + 1] << 16);
-    }
-    float x[16];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      x[2 * j] = bf16_lo(w[j]);
-      x[2 * j + 1] = bf16_hi(w[j]);
-    }
-    // amax over the tile (NaN sticky, as torch's amax)
-    float amax = 0.0f;
-    bool nan = false;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      float v = fabsf(x[j]);
-      nan |= (v != v);
-      amax = fmaxf(amax, v);
-    }
-#pragma unroll
-    for (int off = 1; off < 8; off <<= 1) {
-      amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
-      nan |= __shfl_xor_sync(0xFFFFFFFFu, (int)nan, off) != 0;
-    }
-    float scale = nan ? __uint_as_float(0x7FC00000u) : __fdiv_rn(amax, 448.0f);
-    if (!nan && scale < 1.1754944e-38f) scale = 1.1754944e-38f;
-    uint32_t q[4];
-    if (scale < INFINITY) {  // finite: no NaN or inf in the tile
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        q[j] = f32x2_to_e4m3x2(__fdiv_rn(x[4 * j + 0], scale), __fdiv_rn(x[4 * j + 1], scale)) |
-               (f32x2_to_e4m3x2(__fdiv_rn(x[4 * j + 2], scale), __fdiv_rn(x[4 * j + 3], scale)) << 16);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t b0 = f32_to_e4m3(__fdiv_rn(x[4 * j + 0], scale));
-        uint32_t b1 = f32_to_e4m3(__fdiv_rn(x[4 * j + 1], scale));
-        uint32_t b2 = f32_to_e4m3(__fdiv_rn(x[4 * j + 2], scale));
-        uint32_t b3 = f32_to_e4m3(__fdiv_rn(x[4 * j + 3], scale));
-        q[j] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+      for (int j = 0; j < 8; ++j) {
+        x[2 * j] = bf16_lo(cur.w[j]);
+        x[2 * j + 1] = bf16_hi(cur.w[j]);
       }
-    }
-    uint8_t* row = cache + slot * (int64_t)kRowBytes;
-    reinterpret_cast<uint4*>(row)[lane] = make_uint4(q[0], q[1], q[2], q[3]);
-    if ((lane & 7) == 0) reinterpret_cast<float*>(row + kScaleOff)[lane >> 3] = scale;
-    if (lane < 8) {
-      const uint16_t* r = k_pe + tok * k_pe_stride + lane * 8;
-      uint4 p;
-      if ((k_pe_stride % 8) == 0 && (reinterpret_cast<uintptr_t>(k_pe) & 15) == 0) {
-        p = *reinterpret_cast<const uint4*>(r);
+      // amax over the tile (NaN sticky, as torch's amax)
+      float amax = 0.0f;
+      bool nan = false;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float v = fabsf(x[j]);
+        nan |= (v != v);
+        amax = fmaxf(amax, v);
+      }
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
+        nan |= __shfl_xor_sync(0xFFFFFFFFu, (int)nan, off) != 0;
+      }
+      float scale = nan ? __uint_as_float(0x7FC00000u) : __fdiv_rn(amax, 448.0f);
+      if (!nan && scale < 1.1754944e-38f) scale = 1.1754944e-38f;
+      uint32_t q[4];
+      if (scale < INFINITY) {  // finite: no NaN or inf in the tile
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          q[j] = f32x2_to_e4m3x2(__fdiv_rn(x[4 * j + 0], scale), __fdiv_rn(x[4 * j + 1], scale)) |
+                 (f32x2_to_e4m3x2(__fdiv_rn(x[4 * j + 2], scale), __fdiv_rn(x[4 * j + 3], scale)) << 16);
       } else {
-        p.x = (uint32_t)r[0] | ((uint32_t)r[1] << 16);
-        p.y = (uint32_t)r[2] | ((uint32_t)r[3] << 16);
-        p.z = (uint32_t)r[4] | ((uint32_t)r[5] << 16);
-        p.w = (uint32_t)r[6] | ((uint32_t)r[7] << 16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t b0 = f32_to_e4m3(__fdiv_rn(x[4 * j + 0], scale));
+          uint32_t b1 = f32_to_e4m3(__fdiv_rn(x[4 * j + 1], scale));
+          uint32_t b2 = f32_to_e4m3(__fdiv_rn(x[4 * j + 2], scale));
+          uint32_t b3 = f32_to_e4m3(__fdiv_rn(x[4 * j + 3], scale));
+          q[j] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        }
       }
-      reinterpret_cast<uint4*>(row + kRopeOff)[lane] = p;
+      uint8_t* row = cache + slot * (int64_t)kRowBytes;
+      reinterpret_cast<uint4*>(row)[lane] = make_uint4(q[0], q[1], q[2], q[3]);
+      if ((lane & 7) == 0) reinterpret_cast<float*>(row + kScaleOff)[lane >> 3] = scale;
+      if (lane < 8) reinterpret_cast<uint4*>(row + kRopeOff)[lane] = cur.rope;
     }
+    cur = nxt;
   }
 }
 
