@@ -98,6 +98,7 @@ constexpr int kVStageBytes = 4 * kVBlockBytes;
 constexpr int kVStages = 2;
 constexpr int kPStageBytes = 64 * 128;    // 64 heads x 64 tokens bf16
 constexpr int kPStages = 2;
+static_assert(kKStages == 2 && kVStages == kPStages, "S / K and P / V completions share barriers");
 // raw ring: a stage is one tile's 32 own rows, 8 gather4 groups of 4 rows
 constexpr int kGroupBytes = 2688;         // 4 whole rows (2624 B), 128-B multiple
 constexpr int kRawStageBytes = 8 * kGroupBytes;
@@ -132,7 +133,8 @@ struct Smem {
   uint32_t vmask[kMaskSlots][2];            // tile rows [0,32) and [32,64) live bits
   uint64_t raw_full[kRawStages], raw_empty[kRawStages];
   uint64_t kready[kKStages], vready[kVStages];  // even CTA: tile j's K / V rows in both CTAs
-  uint64_t kempty[kKStages], vempty[kVStages];
+  // one commit per MMA group: QK(j) done frees K stage j % 2 and fills S
+  // buffer j % 2; PV(j) done frees P and V stage j % 2
   uint64_t sfull[2], pfull[kPStages], pempty[kPStages];
   uint64_t xch[2];
   uint64_t mfull[kMaskSlots];               // this CTA: the tile's live bits written
@@ -203,8 +205,7 @@ __device__ void mma_role(const Ctx& c) {
         mma_pair_ss(c.tmem + kColO + 128 * hf, pd + (uint64_t)((kk * 32) >> 4),
                     vd + (uint64_t)((hf * 2 * kVBlockBytes + kk * 16 * 128) >> 4), kIdescPV,
                     (jj > 0 || kk > 0) ? 1u : 0u);
-    mma_commit_pair(c.b_pempty + 8 * ps);
-    mma_commit_pair(c.b_vempty + 8 * vs);
+    mma_commit_pair(c.b_pempty + 8 * ps);  // = V stage vs empty
     return true;
   };
   for (int j = 0; j < c.ntiles && ok; ++j) {
@@ -214,8 +215,7 @@ __device__ void mma_role(const Ctx& c) {
     tc_fence_after();
     issue_qk(c.tmem + kColS + kSBufCols * b, tQ, qdesc0,
              kdesc0 + (uint64_t)((ks * kKStageBytes) >> 4));
-    mma_commit_pair(c.b_sfull + 8 * b);
-    mma_commit_pair(c.b_kempty + 8 * ks);
+    mma_commit_pair(c.b_sfull + 8 * b);  // = K stage ks empty
     if (j >= 1) ok = issue_pv(j - 1);
   }
   if (ok && c.ntiles > 0) {
@@ -497,11 +497,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   c.sp0 = smem_u32(s.p[0]);
   c.b_kready = smem_u32(&s.kready[0]);
   c.b_vready = smem_u32(&s.vready[0]);
-  c.b_kempty = smem_u32(&s.kempty[0]);
-  c.b_vempty = smem_u32(&s.vempty[0]);
   c.b_sfull = smem_u32(&s.sfull[0]);
   c.b_pfull = smem_u32(&s.pfull[0]);
   c.b_pempty = smem_u32(&s.pempty[0]);
+  c.b_kempty = c.b_sfull;
+  c.b_vempty = c.b_pempty;
   c.b_xch = smem_u32(&s.xch[0]);
   c.b_qready = smem_u32(&s.qready);
   c.b_ofull = smem_u32(&s.ofull);
@@ -517,11 +517,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < kKStages; ++i) {
       mbar_init(c.b_kready + 8 * i, 2 * kLoadWarps);
-      mbar_init(c.b_kempty + 8 * i, 1);
     }
     for (int i = 0; i < kVStages; ++i) {
       mbar_init(c.b_vready + 8 * i, 2 * kLoadWarps);
-      mbar_init(c.b_vempty + 8 * i, 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(c.b_sfull + 8 * i, 1);
