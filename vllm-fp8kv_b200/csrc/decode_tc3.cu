@@ -48,19 +48,21 @@
 //   p    2 stages: P (bf16) of 64 heads x 64 tokens                   16 KB
 //   raw  2 stages: the tile's 32 own rows as gathered by TMA          42 KB
 //
-// Warp roles (480 threads per CTA; warp w runs on SM sub-partition w % 4):
+// Warp roles (512 threads per CTA; warp w runs on SM sub-partition w % 4):
 //   warps 0-3   softmax + epilogue (thread L = TMEM lane L)
 //   warp 4      TMEM allocation in both CTAs; lane 0 of the even CTA issues
 //               every MMA of the pair
-//   warp 8      producer: indices -> slots (block table included for the
+//   warp 15     producer: indices -> slots (block table included for the
 //               paged entry point) -> gather4 of own rows into the raw ring
 //   warps 5-7, 9-11, 13-14
 //               dequant: part A = the PV half of the 64 tile rows (V stage,
 //               and the K stage for own rows; the other CTA's rows loaded
 //               into registers here), part B = the other half and the rope
 //               of the 32 own rows (K stage)
-//   warp 12     idle (it keeps sub-partition 0, which issues the MMAs, free
-//               of dequant work: 88.0 vs 89.1 us per call at c2)
+//   warps 8, 12 idle: sub-partition 0, which issues the MMAs, runs only the
+//               issuing thread and softmax warp 0 (c2 88.0 vs 89.1 us per
+//               call with a dequant warp there; 82.6 vs 83.9 with the
+//               producer there)
 // Barriers that gate the issuing thread live in the even CTA and count
 // arrivals of both CTAs; pair-MMA completion reaches both CTAs through a
 // multicast commit.  Every wait is bounded; after a failed wait a role stops,
@@ -108,9 +110,9 @@ constexpr int kMaskSlots = 4;
 constexpr int kSoftmaxWarps = 4;
 constexpr int kMmaWarp = 4;
 constexpr int kLoadWarps = 8;
-constexpr int kProducerWarp = 8;
-constexpr int kIdleWarp = 12;
-constexpr int kThreads = 15 * 32;  // 480
+constexpr int kProducerWarp = 15;
+constexpr int kIdleWarp0 = 8, kIdleWarp1 = 12;
+constexpr int kThreads = 16 * 32;  // 512
 // dequant index of warp w (5-7, 9-11, 13-14 -> 0-7)
 __device__ __forceinline__ int dequant_index(int w) { return w < 8 ? w - 5 : w < 12 ? w - 6 : w - 7; }
 constexpr uint32_t kTmemCols = 512;
@@ -190,11 +192,16 @@ __device__ void mma_role(const Ctx& c) {
   const uint64_t kdesc0 = sdesc_sw128(c.sk0, 16, 1024);
   const uint64_t pdesc0 = sdesc_sw128(c.sp0, 16, 1024);
   const uint64_t vdesc0 = sdesc_sw128(c.sv0, kVBlockBytes, 1024);
-  // PV(jj): waits for P(jj) (softmax of both CTAs) and V(jj) (dequant of both)
+  // PV(jj): waits for P(jj) (softmax of both CTAs) and V(jj) (dequant of
+  // both).  Every dequant warp writes and fences V(jj) before its K(jj + 1)
+  // arrival, so once QK(jj + 1) has been issued V(jj) is known to be in place:
+  // only the last tile waits for its V barrier (whose earlier phases have all
+  // completed by then, so the parity names the right one).
   auto issue_pv = [&](int jj) -> bool {
     const int ps = jj % kPStages, vs = jj % kVStages;
     if (!thread_wait_cluster(c.b_pfull + 8 * ps, (jj / kPStages) & 1, 36)) return false;
-    if (!thread_wait_cluster(c.b_vready + 8 * vs, (jj / kVStages) & 1, 38)) return false;
+    if (jj == c.ntiles - 1 && !thread_wait_cluster(c.b_vready + 8 * vs, (jj / kVStages) & 1, 38))
+      return false;
     tc_fence_after();
     const uint64_t pd = pdesc0 + (uint64_t)((ps * kPStageBytes) >> 4);
     const uint64_t vd = vdesc0 + (uint64_t)((vs * kVStageBytes) >> 4);
@@ -724,7 +731,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == kProducerWarp) {
     producer<kPaged>(c, s, &tm_row, lane);
-  } else if (warp != kIdleWarp) {
+  } else if (warp != kIdleWarp0 && warp != kIdleWarp1) {
     dequant_role<kPaged>(c, s, dequant_index(warp), lane);
   }
 
