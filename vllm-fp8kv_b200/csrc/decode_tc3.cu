@@ -49,7 +49,9 @@
 //   raw  2 stages: the tile's 32 own rows as gathered by TMA          42 KB
 //
 // Warp roles (512 threads per CTA; warp w runs on SM sub-partition w % 4):
-//   warps 0-3   softmax + epilogue (thread L = TMEM lane L)
+//   warps 0-3   softmax (thread L = TMEM lane L), row sums and LSE
+//   all warps   epilogue: warp w stores O columns [64 (w / 4), +64) of TMEM
+//               lanes [32 (w % 4), +32)
 //   warp 4      TMEM allocation in both CTAs; lane 0 of the even CTA issues
 //               every MMA of the pair
 //   warp 15     producer: indices -> slots (block table included for the
@@ -131,6 +133,8 @@ struct Smem {
   uint8_t raw[kRawStages][kRawStageBytes];  // gather4 destinations (128-B aligned)
   float pmax[2][128];                       // partial tile max, by tile parity
   float lsum[128];                          // partial row sums (epilogue)
+  float inv[128];                           // 1 / row sum per TMEM lane (epilogue)
+  uint32_t epi_ok[kSoftmaxWarps];           // softmax warp q finished every tile
   uint8_t rvalid[kRawStages][kOwn];         // own row live (producer's flags)
   uint32_t vmask[kMaskSlots][2];            // tile rows [0,32) and [32,64) live bits
   uint64_t raw_full[kRawStages], raw_empty[kRawStages];
@@ -556,7 +560,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t tmem = c.tmem;
 
   if (warp < kSoftmaxWarps) {
-    // ================================================= softmax + epilogue
+    // ================================================= softmax
     const int L = threadIdx.x;          // TMEM lane
     const int m = L & 63, hh = L >> 6;  // head within the CTA, token half of a tile
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
@@ -677,15 +681,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive_cluster(c.b_pfull + 8 * ps, 0);
     }
 
-    // ---- epilogue: the two threads of a head add their row sums
+    // ---- epilogue: the two threads of a head add their row sums; the
+    // output rows are stored below by all warps
     s.lsum[L] = l;
     named_sync(1, kSoftmaxWarps * 32);
     const float lt = l + s.lsum[L ^ 64];
-    const bool have_o = ok && c.ntiles > 0 && warp_wait_cluster(c.b_ofull, 0, 32);
-    if (have_o) tc_fence_after();
-    const float inv = lt > 0.f ? 1.f / lt : 0.f;
     const float lse_v = lt > 0.f ? m_used * kLn2 + logf(lt) : -INFINITY;
+    s.inv[L] = lt > 0.f ? 1.f / lt : 0.f;
+    if (lane == 0) s.epi_ok[warp] = ok ? 1u : 0u;
     const int hh_glob = head0 + m;
+    if (hh == 0 && m < nh) {
+      if (a.num_splits == 1) {
+        if (a.lse != nullptr) a.lse[t * a.lse_st + hh_glob] = lse_v;
+      } else {
+        a.ws_lse[(t * a.H + hh_glob) * a.num_splits + split] = lse_v;
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (rank == 0 && lane == 0) mma_role(c);
+    __syncwarp();
+  } else if (warp == kProducerWarp) {
+    producer<kPaged>(c, s, &tm_row, lane);
+  } else if (warp != kIdleWarp0 && warp != kIdleWarp1) {
+    dequant_role<kPaged>(c, s, dequant_index(warp), lane);
+  }
+
+  // ---- epilogue over all 16 warps: warp w normalises and stores columns
+  // [64 (w / 4), +64) of the O rows in TMEM lanes [32 (w % 4), +32) (a warp
+  // reaches the lanes of its sub-partition only), once PV(last) is complete
+  named_sync(2, kThreads);  // the softmax warps' 1 / l and status are in place
+  {
+    const int qd = warp & 3;
+    const int L = 32 * qd + lane;
+    const int m = L & 63, hh = L >> 6;
+    const bool have_o = s.epi_ok[qd] != 0 && c.ntiles > 0 && warp_wait_cluster(c.b_ofull, 0, 32);
+    if (have_o) tc_fence_after();
+    const float inv = s.inv[L];
+    const int hh_glob = head0 + m;
+    const uint32_t trow = tmem + ((uint32_t)(qd * 32) << 16);
     auto store32 = [&](const uint32_t (&o)[32], int c0) {
       const int d = 256 * (c0 >> 7) + 128 * hh + (c0 & 127);
       uint4* dst = a.num_splits == 1
@@ -703,36 +736,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
       }
     };
-#pragma unroll 1
-    for (int c0 = 0; c0 < 256; c0 += 64) {
-      uint32_t o0[32], o1[32];
-      if (have_o) {
-        tmem_ld32(trow + kColO + c0, o0);
-        tmem_ld32(trow + kColO + c0 + 32, o1);
-        tmem_wait_ld();
-      } else {
+    const int c0 = 64 * (warp >> 2);
+    uint32_t o0[32], o1[32];
+    if (have_o) {
+      tmem_ld32(trow + kColO + c0, o0);
+      tmem_ld32(trow + kColO + c0 + 32, o1);
+      tmem_wait_ld();
+    } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o0[i] = o1[i] = 0u;
-      }
-      if (m < nh) {
-        store32(o0, c0);
-        store32(o1, c0 + 32);
-      }
+      for (int i = 0; i < 32; ++i) o0[i] = o1[i] = 0u;
     }
-    if (hh == 0 && m < nh) {
-      if (a.num_splits == 1) {
-        if (a.lse != nullptr) a.lse[t * a.lse_st + hh_glob] = lse_v;
-      } else {
-        a.ws_lse[(t * a.H + hh_glob) * a.num_splits + split] = lse_v;
-      }
+    if (m < nh) {
+      store32(o0, c0);
+      store32(o1, c0 + 32);
     }
-  } else if (warp == kMmaWarp) {
-    if (rank == 0 && lane == 0) mma_role(c);
-    __syncwarp();
-  } else if (warp == kProducerWarp) {
-    producer<kPaged>(c, s, &tm_row, lane);
-  } else if (warp != kIdleWarp0 && warp != kIdleWarp1) {
-    dequant_role<kPaged>(c, s, dequant_index(warp), lane);
   }
 
   // both CTAs: no MMA of the pair may still run, no arrival may still target
