@@ -299,8 +299,10 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
     torch.cuda.synchronize(dev)
     w0.record(stream)
+    h0 = time.perf_counter()
     for i in range(args.steps):
         step(i)
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # enqueue cost per call
     w1.record(stream)
     torch.cuda.synchronize(dev)
     if dist:
@@ -416,6 +418,7 @@ def run_ours(args, rank, world, local_rank):
                                + (" (decode + merge launches)" if launches_per_step > 1 else ""))
         roof["kernel_us"] = step_ms * 1e3
         roof["launch_us"] = launch_ms * 1e3
+        roof["host_enqueue_us"] = host_ms * 1e3
         roof["traffic"] = _traffic_per_launch(kern, args.workload)
         roof["algorithmic_bytes_per_launch"] = alg
         roof["algorithmic_flops_per_launch"] = flops
