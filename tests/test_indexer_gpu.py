@@ -162,6 +162,19 @@ def test_indexer_topk_rows_longer_than_the_resident_limit(cuda_device):
     assert np.array_equal(top, O.indexer_topk(lg, 1, ctx, 2048))
 
 
+def test_indexer_topk_rows_at_the_pair_limit(cuda_device):
+    """Rows of exactly 92,160 positions, the longest the CTA pair keeps in
+    shared memory (46 K keys per CTA), and one position more (the single-CTA
+    kernel), in one call each: both equal the oracle, ties included."""
+    rng = np.random.default_rng(16)
+    for L in (92160, 92161):
+        lg = rng.standard_normal((2, L)).astype(np.float32)
+        lg[1, ::5] = 0.75  # a tie class near the threshold
+        ctx = np.array([L, L - 1], np.int32)
+        top = indexer_topk(torch.from_numpy(lg).cuda(), 1, torch.from_numpy(ctx).cuda(), 2048).cpu().numpy()
+        assert np.array_equal(top, O.indexer_topk(lg, 1, ctx, 2048)), L
+
+
 def test_indexer_topk_row_in_one_first_pass_bin(cuda_device):
     """Every logit in [1, 1.25) shares the first pass's 11-bit bin, more keys
     than the compacted candidate list holds: the refining passes then scan the
@@ -176,7 +189,7 @@ def test_indexer_topk_row_in_one_first_pass_bin(cuda_device):
 
 
 def test_indexer_topk_rows_above_the_pair_limit(cuda_device):
-    """Rows of more than 96,256 positions take the single-CTA kernel that
+    """Rows of more than 92,160 positions take the single-CTA kernel that
     re-reads the row per pass; a short row in the same call leaves early."""
     rng = np.random.default_rng(14)
     L = 100000

@@ -30,7 +30,7 @@
 // the MMAs of tile t+1.  Every wait is bounded (status word, as the decode).
 //
 // Top-k: a 2-CTA cluster per logits row (one CTA per row for rows above
-// 96,256 positions).  Logits map to order-preserving 32-bit keys, kept in
+// 92,160 positions).  Logits map to order-preserving 32-bit keys, kept in
 // shared memory (each CTA its half of the row); three histogram passes (11, 11
 // and 10 bits, the two CTAs' counts added through distributed shared memory)
 // find the k-th largest key exactly; a final pass in position order writes
@@ -414,7 +414,7 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* warp_s
 // positions' keys in shared memory (192 KB), so the row is read from global
 // memory once.  Longer rows take the single-CTA kernel, which re-reads the
 // row for each pass (from L2).
-constexpr int kSmemKeys = 48 * 1024;
+constexpr int kSmemKeys = 46 * 1024;
 constexpr int kCand = 4096;  // compacted candidates of the first pass (16 KB)
 constexpr int64_t kRound = (int64_t)kTopkThreads * 32;  // positions of one write round
 static_assert(kSmemKeys <= 2 * kRound, "a CTA's positions take at most two write rounds");
@@ -434,6 +434,11 @@ __device__ __forceinline__ uint32_t ld_dsmem(uint32_t local, uint32_t rank) {
   asm volatile("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(mapa(local, rank)) : "memory");
   return v;
 }
+// Atomically add v to the 32-bit word at shared::cta address `local` of
+// cluster CTA `rank`.
+__device__ __forceinline__ void red_add_dsmem(uint32_t local, uint32_t rank, uint32_t v) {
+  asm volatile("red.shared::cluster.add.u32 [%0], %1;\n" ::"r"(mapa(local, rank)), "r"(v) : "memory");
+}
 
 // Top-k of one row on a CTA pair (rows up to kPairMaxLen).  Each CTA loads and
 // converts its half of the row; the three histogram passes add the two CTAs'
@@ -446,7 +451,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
                              int64_t max_len) {
   extern __shared__ uint32_t skeys[];  // keys of this CTA's positions
   __shared__ uint32_t hist[2048];      // this CTA's counts
-  __shared__ uint32_t hsum[2048];      // both CTAs' counts
+  __shared__ uint32_t hsum[2][2048];   // both CTAs' counts, by pass parity
   __shared__ uint32_t warp_sums[32];
   __shared__ uint32_t sel[2];          // chosen bin, keys above it (this pass)
   __shared__ uint32_t cand[kCand];     // this CTA's positions in the first pass's bin
@@ -471,30 +476,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
   const float* rowl = row + base;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t lt = (1u << lane) - 1u;
-  // both CTAs' counts of the first nbins bins -> hsum (the first barrier: both
-  // histograms are complete; the second: the peer has read this one)
-  auto merge = [&](int nbins) {
-    cluster_sync_all();
-    for (int i = threadIdx.x; i < nbins; i += kTopkThreads)
-      hsum[i] = hist[i] + ld_dsmem(smem_u32(&hist[i]), peer);
+  // both CTAs' counts of the first nbins bins -> hsum[b] of both CTAs: each
+  // CTA adds its counts into its own and its peer's copy, and one cluster
+  // barrier completes them.  The other buffer, read last in the previous
+  // pass, is zeroed first, before the barrier after which the peer may add
+  // the next pass's counts into it.
+  auto merge = [&](int nbins, int b) {
+    __syncthreads();  // this CTA's histogram is complete
+    for (int i = threadIdx.x; i < 2048; i += kTopkThreads) hsum[b ^ 1][i] = 0;
+    for (int i = threadIdx.x; i < nbins; i += kTopkThreads) {
+      const uint32_t v = hist[i];
+      if (v != 0) {
+        atomicAdd(&hsum[b][i], v);
+        red_add_dsmem(smem_u32(&hsum[b][i]), peer, v);
+      }
+    }
     cluster_sync_all();
   };
   // The bin holding the `rem`-th largest counted key (bins taken from the
   // top): thread t owns nbins / 1024 bins and one block scan orders the
   // threads.  Leaves the bin and the count above it in sel[0], sel[1].
-  auto select_bin = [&](int nbins, uint32_t rem) {
+  auto select_bin = [&](int nbins, uint32_t rem, int b) {
+    const uint32_t* hs = hsum[b];
     const int per = nbins / kTopkThreads;
     const int hi = nbins - per * (int)threadIdx.x;
     uint32_t sum = 0;
-    for (int bi = hi - 1; bi >= hi - per; --bi) sum += hsum[bi];
+    for (int bi = hi - 1; bi >= hi - per; --bi) sum += hs[bi];
     uint32_t tot;
     const uint32_t ex = block_excl_scan(sum, warp_sums, &tot);
     if (ex < rem && ex + sum >= rem) {
       uint32_t above = ex;
       int bi = hi - 1;
       for (; bi > hi - per; --bi) {
-        if (above + hsum[bi] >= rem) break;
-        above += hsum[bi];
+        if (above + hs[bi] >= rem) break;
+        above += hs[bi];
       }
       sel[0] = (uint32_t)bi;
       sel[1] = above;
@@ -505,12 +520,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
   // all of a thread's in flight at once; unaligned rows and the ragged tail
   // element by element), converted to keys in place while the first pass's
   // histogram (top 11 bits) is counted
-  for (int i = threadIdx.x; i < 2048; i += kTopkThreads) hist[i] = 0;
+  for (int i = threadIdx.x; i < 2048; i += kTopkThreads) {
+    hist[i] = 0;
+    hsum[0][i] = 0;
+  }
   __syncthreads();
   const int64_t n4 = (reinterpret_cast<uintptr_t>(rowl) & 15u) == 0 ? nloc >> 2 : 0;
   for (int64_t i = threadIdx.x; i < n4; i += kTopkThreads)
     cp_async16(smem_u32(&skeys[4 * i]), rowl + 4 * i, 16);
   cp_async_commit();
+  cluster_sync_all();  // both CTAs' first count buffer is zero before either adds into it
   for (int64_t i = 4 * n4 + threadIdx.x; i < nloc; i += kTopkThreads) {
     const uint32_t key = sortable_key(rowl[i]);
     skeys[i] = key;
@@ -528,9 +547,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
     atomicAdd(&hist[v.z >> 21], 1u);
     atomicAdd(&hist[v.w >> 21], 1u);
   }
-  merge(2048);
+  merge(2048, 0);
   uint32_t remaining = (uint32_t)k;
-  select_bin(2048, remaining);
+  select_bin(2048, remaining, 0);
   const uint32_t bin0 = sel[0];
   const bool fits = hist[bin0] <= (uint32_t)kCand;  // this CTA's keys of the bin fit the list
   uint32_t prefix = bin0 << 21, pmask = 0x7FFu << 21;
@@ -583,8 +602,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
         if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & (nbins - 1)], 1u);
       }
     }
-    merge(nbins);
-    select_bin(nbins, remaining);
+    merge(nbins, pass & 1);
+    select_bin(nbins, remaining, pass & 1);
     prefix |= sel[0] << shift;
     pmask |= (uint32_t)(nbins - 1) << shift;
     remaining -= sel[1];
