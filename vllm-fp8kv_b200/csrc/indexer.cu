@@ -557,7 +557,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
   // ---- in the write pass's mapping (warp w: local positions [32 S w,
   // 32 S (w + 1)), lane l position 32 j + l at step j < S): per warp, the
   // keys above the bin; the bin's positions into the candidates
-  const int S = (int)((nloc + 1023) / 1024);  // steps per warp, <= 48
+  const int S = (int)((nloc + 1023) / 1024);  // steps per warp, <= 46
   const int64_t wspan = 32 * (int64_t)S;
   const int64_t wb = (int64_t)warp * wspan;
   if (threadIdx.x == 0) ncand = 0;
@@ -660,7 +660,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
   cluster_sync_all();  // CTA 0's totals are read before it may exit
   // ---- write: ascending positions above the k-th key and the first
   // `remaining` equal to it (lim > k: exactly k in all).  This CTA's counts
-  // are below 2^16 (<= 48 K positions), so one packed scan orders the warps.
+  // are below 2^16 (<= 46 K positions), so one packed scan orders the warps.
   {
     const uint32_t cg = gabove[warp] + cgt[warp], ce = ceq[warp];
     uint32_t tot;
