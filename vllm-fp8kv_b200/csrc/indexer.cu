@@ -428,11 +428,9 @@ __host__ __device__ constexpr int64_t pair_half(int64_t lim) {
 constexpr int64_t kPairMaxLen = 2 * (int64_t)kSmemKeys - 2048;
 static_assert(pair_half(kPairMaxLen) <= kSmemKeys, "");
 
-// A 32-bit word at shared::cta address `local` of cluster CTA `rank`.
-__device__ __forceinline__ uint32_t ld_dsmem(uint32_t local, uint32_t rank) {
-  uint32_t v;
-  asm volatile("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(mapa(local, rank)) : "memory");
-  return v;
+// Store v to the 32-bit word at shared::cta address `local` of cluster CTA `rank`.
+__device__ __forceinline__ void st_dsmem(uint32_t local, uint32_t rank, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;\n" ::"r"(mapa(local, rank)), "r"(v) : "memory");
 }
 // Atomically add v to the 32-bit word at shared::cta address `local` of
 // cluster CTA `rank`.
@@ -457,7 +455,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
   __shared__ uint32_t cand[kCand];     // this CTA's positions in the first pass's bin
   __shared__ uint32_t ncand;
   __shared__ uint32_t gabove[32], cgt[32], ceq[32];  // per warp range
-  __shared__ uint32_t tot_ge[2];       // this CTA's keys above / equal to the k-th key
+  __shared__ uint32_t tot_ge[2];       // CTA 1: CTA 0's keys above / equal to the k-th key
   if (threadIdx.x == 0) pdl_launch_dependents();
   pdl_wait();
   const uint32_t peer = cluster_rank() ^ 1u;
@@ -638,8 +636,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
     }
   }
   __syncthreads();
-  // ---- this CTA's totals; CTA 1's output starts after CTA 0's
-  if (warp == 0) {
+  // ---- CTA 1's output starts after CTA 0's: CTA 0 stores its totals into
+  // CTA 1's shared memory, and one cluster barrier (release / acquire)
+  // completes the stores before CTA 1 reads them or CTA 0 exits
+  if (warp == 0 && peer == 1) {
     uint32_t tg = gabove[lane] + cgt[lane], te = ceq[lane];
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
@@ -647,17 +647,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
       te += __shfl_xor_sync(0xFFFFFFFFu, te, off);
     }
     if (lane == 0) {
-      tot_ge[0] = tg;
-      tot_ge[1] = te;
+      st_dsmem(smem_u32(&tot_ge[0]), 1, tg);
+      st_dsmem(smem_u32(&tot_ge[1]), 1, te);
     }
   }
   cluster_sync_all();
-  uint32_t base_g = 0, base_e = 0;
-  if (peer == 0) {
-    base_g = ld_dsmem(smem_u32(&tot_ge[0]), 0);
-    base_e = ld_dsmem(smem_u32(&tot_ge[1]), 0);
-  }
-  cluster_sync_all();  // CTA 0's totals are read before it may exit
+  const uint32_t base_g = peer == 0 ? tot_ge[0] : 0u, base_e = peer == 0 ? tot_ge[1] : 0u;
   // ---- write: ascending positions above the k-th key and the first
   // `remaining` equal to it (lim > k: exactly k in all).  This CTA's counts
   // are below 2^16 (<= 46 K positions), so one packed scan orders the warps.
