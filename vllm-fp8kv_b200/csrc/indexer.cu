@@ -432,11 +432,6 @@ static_assert(pair_half(kPairMaxLen) <= kSmemKeys, "");
 __device__ __forceinline__ void st_dsmem(uint32_t local, uint32_t rank, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;\n" ::"r"(mapa(local, rank)), "r"(v) : "memory");
 }
-// Atomically add v to the 32-bit word at shared::cta address `local` of
-// cluster CTA `rank`.
-__device__ __forceinline__ void red_add_dsmem(uint32_t local, uint32_t rank, uint32_t v) {
-  asm volatile("red.shared::cluster.add.u32 [%0], %1;\n" ::"r"(mapa(local, rank)), "r"(v) : "memory");
-}
 
 // Top-k of one row on a CTA pair (rows up to kPairMaxLen).  Each CTA loads and
 // converts its half of the row; the three histogram passes add the two CTAs'
@@ -449,7 +444,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
                              int64_t max_len) {
   extern __shared__ uint32_t skeys[];  // keys of this CTA's positions
   __shared__ uint32_t hist[2048];      // this CTA's counts
-  __shared__ uint32_t hsum[2][2048];   // both CTAs' counts, by pass parity
+  __shared__ uint32_t hpeer[2][2048];  // the peer CTA's counts, by pass parity
   __shared__ uint32_t warp_sums[32];
   __shared__ uint32_t sel[2];          // chosen bin, keys above it (this pass)
   __shared__ uint32_t cand[kCand];     // this CTA's positions in the first pass's bin
@@ -474,40 +469,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
   const float* rowl = row + base;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t lt = (1u << lane) - 1u;
-  // both CTAs' counts of the first nbins bins -> hsum[b] of both CTAs: each
-  // CTA adds its counts into its own and its peer's copy, and one cluster
-  // barrier completes them.  The other buffer, read last in the previous
-  // pass, is zeroed first, before the barrier after which the peer may add
-  // the next pass's counts into it.
+  // each CTA stores its counts of the first nbins bins into its peer's
+  // hpeer[b], and one cluster barrier completes the stores.  The buffers
+  // alternate by pass: the peer stores into hpeer[b] again two passes later,
+  // after the barrier of the pass in between, which follows this CTA's last
+  // read of it.
   auto merge = [&](int nbins, int b) {
     __syncthreads();  // this CTA's histogram is complete
-    for (int i = threadIdx.x; i < 2048; i += kTopkThreads) hsum[b ^ 1][i] = 0;
-    for (int i = threadIdx.x; i < nbins; i += kTopkThreads) {
-      const uint32_t v = hist[i];
-      if (v != 0) {
-        atomicAdd(&hsum[b][i], v);
-        red_add_dsmem(smem_u32(&hsum[b][i]), peer, v);
-      }
-    }
+    for (int i = threadIdx.x; i < nbins; i += kTopkThreads) st_dsmem(smem_u32(&hpeer[b][i]), peer, hist[i]);
     cluster_sync_all();
   };
   // The bin holding the `rem`-th largest counted key (bins taken from the
   // top): thread t owns nbins / 1024 bins and one block scan orders the
   // threads.  Leaves the bin and the count above it in sel[0], sel[1].
   auto select_bin = [&](int nbins, uint32_t rem, int b) {
-    const uint32_t* hs = hsum[b];
+    const uint32_t* hp = hpeer[b];
     const int per = nbins / kTopkThreads;
     const int hi = nbins - per * (int)threadIdx.x;
     uint32_t sum = 0;
-    for (int bi = hi - 1; bi >= hi - per; --bi) sum += hs[bi];
+    for (int bi = hi - 1; bi >= hi - per; --bi) sum += hist[bi] + hp[bi];
     uint32_t tot;
     const uint32_t ex = block_excl_scan(sum, warp_sums, &tot);
     if (ex < rem && ex + sum >= rem) {
       uint32_t above = ex;
       int bi = hi - 1;
       for (; bi > hi - per; --bi) {
-        if (above + hs[bi] >= rem) break;
-        above += hs[bi];
+        if (above + hist[bi] + hp[bi] >= rem) break;
+        above += hist[bi] + hp[bi];
       }
       sel[0] = (uint32_t)bi;
       sel[1] = above;
@@ -518,16 +506,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
   // all of a thread's in flight at once; unaligned rows and the ragged tail
   // element by element), converted to keys in place while the first pass's
   // histogram (top 11 bits) is counted
-  for (int i = threadIdx.x; i < 2048; i += kTopkThreads) {
-    hist[i] = 0;
-    hsum[0][i] = 0;
-  }
+  for (int i = threadIdx.x; i < 2048; i += kTopkThreads) hist[i] = 0;
   __syncthreads();
   const int64_t n4 = (reinterpret_cast<uintptr_t>(rowl) & 15u) == 0 ? nloc >> 2 : 0;
   for (int64_t i = threadIdx.x; i < n4; i += kTopkThreads)
     cp_async16(smem_u32(&skeys[4 * i]), rowl + 4 * i, 16);
   cp_async_commit();
-  cluster_sync_all();  // both CTAs' first count buffer is zero before either adds into it
   for (int64_t i = 4 * n4 + threadIdx.x; i < nloc; i += kTopkThreads) {
     const uint32_t key = sortable_key(rowl[i]);
     skeys[i] = key;
