@@ -468,7 +468,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
   const int64_t nloc = max((int64_t)0, min(lim - base, half));  // positions [base, base + nloc)
   const float* rowl = row + base;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t lt = (1u << lane) - 1u;
   // each CTA stores its counts of the first nbins bins into its peer's
   // hpeer[b], and one cluster barrier completes the stores.  The buffers
   // alternate by pass: the peer stores into hpeer[b] again two passes later,
@@ -536,32 +535,76 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
   const bool fits = hist[bin0] <= (uint32_t)kCand;  // this CTA's keys of the bin fit the list
   uint32_t prefix = bin0 << 21, pmask = 0x7FFu << 21;
   remaining -= sel[1];
-  // ---- in the write pass's mapping (warp w: local positions [32 S w,
-  // 32 S (w + 1)), lane l position 32 j + l at step j < S): per warp, the
-  // keys above the bin; the bin's positions into the candidates
-  const int S = (int)((nloc + 1023) / 1024);  // steps per warp, <= 46
-  const int64_t wspan = 32 * (int64_t)S;
-  const int64_t wb = (int64_t)warp * wspan;
-  if (threadIdx.x == 0) ncand = 0;
-  __syncthreads();
+  // ---- the write pass's mapping: warp w owns local positions [wspan w,
+  // wspan (w + 1)) in groups of 128, lane l positions 4 l .. 4 l + 3 of a
+  // group (one 16-byte shared-memory load).  Per warp: the keys above the
+  // bin and in it; then the bin's positions into the candidates at the
+  // warp's offset (a block scan, no atomics)
+  const int G4 = (int)((nloc + 4095) / 4096);  // groups per warp, <= 12
+  const int wspan = 128 * G4;
+  const int wb = warp * wspan;
+  const int nl = (int)nloc;
+  // group gi's four keys of this lane and how many of them are positions < nloc
+  auto load4 = [&](int gi, uint32_t (&kk)[4]) -> int {
+    const int p0 = wb + 128 * gi + 4 * lane;
+    if (p0 >= nl) {
+      kk[0] = kk[1] = kk[2] = kk[3] = 0u;
+      return 0;
+    }
+    const uint4 v = *reinterpret_cast<const uint4*>(&skeys[p0]);  // p0 + 4 <= the CTA's share
+    kk[0] = v.x;
+    kk[1] = v.y;
+    kk[2] = v.z;
+    kk[3] = v.w;
+    return min(4, nl - p0);
+  };
+  // exclusive prefix over the warp's lanes, and the warp's total
+  auto warp_excl = [&](uint32_t v, uint32_t& total) -> uint32_t {
+    uint32_t x = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, off);
+      if (lane >= off) x += y;
+    }
+    total = __shfl_sync(0xFFFFFFFFu, x, 31);
+    return x - v;
+  };
   {
-    uint32_t ga = 0;
-#pragma unroll 4
-    for (int j = 0; j < S; ++j) {
-      const int64_t i = wb + 32 * j + lane;
-      const bool v = i < nloc;
-      const uint32_t top = v ? skeys[i] >> 21 : 0u;
-      ga += __popc(__ballot_sync(0xFFFFFFFFu, v && top > bin0));
-      if (fits) {
-        const bool m = v && top == bin0;
-        const uint32_t bal = __ballot_sync(0xFFFFFFFFu, m);
-        uint32_t cb = 0;
-        if (lane == 0 && bal != 0) cb = atomicAdd(&ncand, (uint32_t)__popc(bal));
-        cb = __shfl_sync(0xFFFFFFFFu, cb, 0);
-        if (m) cand[cb + __popc(bal & lt)] = (uint32_t)i;
+    uint32_t ga = 0, gb = 0;
+    for (int gi = 0; gi < G4; ++gi) {
+      uint32_t kk[4];
+      const int nv = load4(gi, kk);
+      uint32_t ca = 0, cb = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t top = kk[q] >> 21;
+        ca += (q < nv && top > bin0) ? 1u : 0u;
+        cb += (q < nv && top == bin0) ? 1u : 0u;
       }
+      ga += __reduce_add_sync(0xFFFFFFFFu, ca);
+      gb += __reduce_add_sync(0xFFFFFFFFu, cb);
     }
     if (lane == 0) gabove[warp] = ga;
+    if (fits) {
+      uint32_t tot;
+      uint32_t cbase = block_excl_scan(lane == 0 ? gb : 0u, warp_sums, &tot);
+      cbase = __shfl_sync(0xFFFFFFFFu, cbase, 0);
+      if (threadIdx.x == 0) ncand = tot;
+      for (int gi = 0; gi < G4; ++gi) {
+        uint32_t kk[4];
+        const int nv = load4(gi, kk);
+        uint32_t m = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) m |= (q < nv && (kk[q] >> 21) == bin0) ? 1u << q : 0u;
+        uint32_t wt;
+        uint32_t at = cbase + warp_excl((uint32_t)__popc(m), wt);
+        const uint32_t p0 = (uint32_t)(wb + 128 * gi + 4 * lane);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if ((m >> q) & 1u) cand[at++] = p0 + q;
+        cbase += wt;
+      }
+    }
   }
   __syncthreads();
   // ---- the two refining passes over the bin's keys (or, when this CTA's did
@@ -601,19 +644,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
   if (fits) {
     for (int c = threadIdx.x; c < nc; c += kTopkThreads) {
       const uint32_t pos = cand[c], key = skeys[pos];
-      const int ww = (int)(pos / wspan);
+      const int ww = (int)pos / wspan;
       if (key > prefix) atomicAdd(&cgt[ww], 1u);
       else if (key == prefix) atomicAdd(&ceq[ww], 1u);
     }
   } else {
     uint32_t cg = 0, ce = 0;
-#pragma unroll 4
-    for (int j = 0; j < S; ++j) {
-      const int64_t i = wb + 32 * j + lane;
-      const uint32_t key = i < nloc ? skeys[i] : 0u;
-      cg += __popc(__ballot_sync(0xFFFFFFFFu, i < nloc && key > prefix && (key >> 21) == bin0));
-      ce += __popc(__ballot_sync(0xFFFFFFFFu, i < nloc && key == prefix));
+    for (int gi = 0; gi < G4; ++gi) {
+      uint32_t kk[4];
+      const int nv = load4(gi, kk);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        cg += (q < nv && kk[q] > prefix && (kk[q] >> 21) == bin0) ? 1u : 0u;
+        ce += (q < nv && kk[q] == prefix) ? 1u : 0u;
+      }
     }
+    cg = __reduce_add_sync(0xFFFFFFFFu, cg);
+    ce = __reduce_add_sync(0xFFFFFFFFu, ce);
     if (lane == 0) {
       cgt[warp] = cg;
       ceq[warp] = ce;
@@ -646,17 +693,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads)
     const uint32_t ex = block_excl_scan(lane == 0 ? ((cg << 16) | ce) : 0u, warp_sums, &tot);
     const uint32_t exw = __shfl_sync(0xFFFFFFFFu, ex, 0);
     uint32_t g = base_g + (exw >> 16), e = base_e + (exw & 0xFFFFu);
-#pragma unroll 4
-    for (int j = 0; j < S; ++j) {
-      const int64_t i = wb + 32 * j + lane;
-      const uint32_t key = i < nloc ? skeys[i] : 0u;
-      const bool isg = i < nloc && key > prefix, ise = i < nloc && key == prefix;
-      const uint32_t bg = __ballot_sync(0xFFFFFFFFu, isg), be = __ballot_sync(0xFFFFFFFFu, ise);
-      const uint32_t gb = g + __popc(bg & lt), eb = e + __popc(be & lt);
-      if (isg) o[gb + min(eb, remaining)] = (int32_t)(base + i);
-      else if (ise && eb < remaining) o[gb + eb] = (int32_t)(base + i);
-      g += __popc(bg);
-      e += __popc(be);
+    for (int gi = 0; gi < G4; ++gi) {
+      uint32_t kk[4];
+      const int nv = load4(gi, kk);
+      uint32_t mg = 0, me = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        mg |= (q < nv && kk[q] > prefix) ? 1u << q : 0u;
+        me |= (q < nv && kk[q] == prefix) ? 1u << q : 0u;
+      }
+      // lanes in order, then a lane's four positions in order (counts of a
+      // group are at most 128, so the two counts share one scan)
+      uint32_t wt;
+      const uint32_t ex4 = warp_excl(((uint32_t)__popc(mg) << 16) | (uint32_t)__popc(me), wt);
+      uint32_t gg = g + (ex4 >> 16), ee = e + (ex4 & 0xFFFFu);
+      const int64_t p0 = base + wb + 128 * gi + 4 * lane;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if ((mg >> q) & 1u) {
+          o[gg + min(ee, remaining)] = (int32_t)(p0 + q);
+          ++gg;
+        } else if ((me >> q) & 1u) {
+          if (ee < remaining) o[gg + ee] = (int32_t)(p0 + q);
+          ++ee;
+        }
+      }
+      g += wt >> 16;
+      e += wt & 0xFFFFu;
     }
   }
 }
