@@ -24,7 +24,8 @@
 //   warps 0-3  epilogue: relu, weights, sum, scale, mask, store (coalesced)
 //   warp 4     producer: block ids from the block table, TMA copies of each
 //              block's values (one 3-D box, 128-byte swizzled) and a bulk copy
-//              of its 64 scales into a 5-stage ring
+//              of its 64 scales into a ring of five stages (four when
+//              next_n is 2); the epilogue warps release a stage
 //   warp 5     tensor memory allocation; lane 0 issues the MMAs
 // Two accumulator buffers in tensor memory let the epilogue of tile t overlap
 // the MMAs of tile t+1.  Every wait is bounded (status word, as the decode).
@@ -54,9 +55,13 @@ constexpr int kHeads = 64;                // index heads per query token
 constexpr int kBlock = 64;                // tokens per cache block
 constexpr int kPageBytes = kBlock * (kDim + 4);   // 8448
 constexpr int kTileTokens = 128;          // MMA M: two blocks
-constexpr int kStages = 4;
 constexpr int kStageBytes = kTileTokens * kDim;   // 16 KB of values
-constexpr int kMaxNextN = 2;              // N = 64 * next_n query heads <= 128
+// The logits kernel is built for NN = 1 (decode) and NN = 2 (next_n 2) query
+// tokens per request (N = 64 NN query heads <= 128; the C ABI refuses larger
+// next_n): with one token's query rows the key ring has five stages in the
+// shared memory that two CTAs per SM leave, with two tokens' four.
+template <int NN>
+constexpr int stages_for() { return NN == 1 ? 5 : 4; }
 constexpr int kThreads = 6 * 32;
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
@@ -67,19 +72,24 @@ __host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
   return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+template <int NN>
 struct Smem {
+  static constexpr int kStages = stages_for<NN>();
   uint8_t kv[kStages][kStageBytes];        // 1024-aligned: swizzled operand tiles
-  uint8_t q[2][kMaxNextN * kHeads * kDim]; // 1024-aligned: N rows of 128 B, swizzled, by item parity
+  uint8_t q[2][NN * kHeads * kDim];        // 1024-aligned: N rows of 128 B, swizzled, by item parity
   float scale[kStages][kTileTokens];
-  float w[2][kMaxNextN * kHeads];          // by item parity
+  float w[2][NN * kHeads];                 // by item parity
   uint8_t pvalid[kStages][2];              // block p of the stage's tile was loaded
   uint64_t full[kStages], empty[kStages];
   uint64_t tfull[2], tempty[2];
   uint64_t qfull[2], qempty[2], drain;
   uint32_t tmem_base;
 };
-static_assert(offsetof(Smem, q) % 1024 == 0, "swizzle atoms need 1024-B alignment");
-static_assert(offsetof(Smem, full) % 8 == 0, "");
+static_assert(offsetof(Smem<1>, q) % 1024 == 0 && offsetof(Smem<2>, q) % 1024 == 0,
+              "swizzle atoms need 1024-B alignment");
+static_assert(offsetof(Smem<1>, full) % 8 == 0 && offsetof(Smem<2>, full) % 8 == 0, "");
+static_assert(2 * (sizeof(Smem<1>) + 1024) <= 228 * 1024 && 2 * (sizeof(Smem<2>) + 1024) <= 228 * 1024,
+              "two CTAs per SM");
 
 struct Args {
   const uint8_t* q;          // [B, next_n, 64, 128] e4m3, contiguous per request
@@ -157,7 +167,9 @@ __device__ __forceinline__ Item item_of(const Args& a, int u) {
   return it;
 }
 
-__device__ void producer(const Args& a, Smem& s, const CUtensorMap* tm) {
+template <int NN>
+__device__ void producer(const Args& a, Smem<NN>& s, const CUtensorMap* tm) {
+  constexpr int kStages = Smem<NN>::kStages;
   int i = 0;
   bool ok = true;
   for (int u = blockIdx.x; u < a.items && ok; u += gridDim.x) {
@@ -195,7 +207,9 @@ __device__ void producer(const Args& a, Smem& s, const CUtensorMap* tm) {
     (void)thread_wait(smem_u32(&s.full[x % kStages]), (x / kStages) & 1, 51);
 }
 
-__device__ void mma_issuer(const Args& a, Smem& s, uint32_t tmem, int N) {
+template <int NN>
+__device__ void mma_issuer(const Args& a, Smem<NN>& s, uint32_t tmem, int N) {
+  constexpr int kStages = Smem<NN>::kStages;
   const uint32_t idesc = idesc_e4m3(kTileTokens, N);
   int i = 0, k = 0;
   bool ok = true;
@@ -217,7 +231,8 @@ __device__ void mma_issuer(const Args& a, Smem& s, uint32_t tmem, int N) {
       for (int kk = 0; kk < kDim / 32; ++kk)  // 32 e4m3 values = 32 bytes per k-step
         mma_f8(tmem + buf * N, adesc + (uint64_t)((kk * 32) >> 4), qdesc + (uint64_t)((kk * 32) >> 4),
                idesc, kk > 0 ? 1u : 0u);
-      mma_commit(smem_u32(&s.empty[st]));
+      // the stage is released by the epilogue warps, which read its scales
+      // after they have seen this commit (so the MMAs are done with it)
       mma_commit(smem_u32(&s.tfull[buf]));
     }
     // this item's query buffer is free once its MMAs complete (at once when
@@ -231,7 +246,8 @@ __device__ void mma_issuer(const Args& a, Smem& s, uint32_t tmem, int N) {
 
 // The request's query rows (swizzled K-major operand) and head weights into
 // buffer qb; announced on qfull[qb] after every epilogue warp's stores.
-__device__ void load_query(const Args& a, Smem& s, int b, int qb, int N, int lane) {
+template <int NN>
+__device__ void load_query(const Args& a, Smem<NN>& s, int b, int qb, int N, int lane) {
   const int nn = a.next_n;
   const uint4* qsrc = reinterpret_cast<const uint4*>(a.q + (int64_t)b * a.q_stride_b);
   for (int c = threadIdx.x; c < N * (kDim / 16); c += 128) {
@@ -245,7 +261,10 @@ __device__ void load_query(const Args& a, Smem& s, int b, int qb, int N, int lan
   if (lane == 0) mbar_arrive(smem_u32(&s.qfull[qb]));
 }
 
-__device__ void epilogue(const Args& a, Smem& s, uint32_t tmem, int N) {
+template <int NN>
+__device__ void epilogue(const Args& a, Smem<NN>& s, uint32_t tmem, int N) {
+  constexpr int kStages = Smem<NN>::kStages;
+  constexpr int kMaxNextN = NN;  // query tokens per request, at most
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = threadIdx.x;  // TMEM lane = token of the tile
   const int nn = a.next_n;
@@ -322,12 +341,14 @@ __device__ void epilogue(const Args& a, Smem& s, uint32_t tmem, int N) {
 
 }  // namespace
 
+template <int NN>
 __global__ void __launch_bounds__(kThreads, 1)
     indexer_logits_kernel(const Args a, const __grid_constant__ CUtensorMap tm) {
+  constexpr int kStages = Smem<NN>::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t pad = ((raw_base + 1023u) & ~1023u) - raw_base;
-  Smem& s = *reinterpret_cast<Smem*>(smem_raw + pad);
+  Smem<NN>& s = *reinterpret_cast<Smem<NN>*>(smem_raw + pad);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = kHeads * a.next_n;
   const uint32_t tmem_cols = N <= 64 ? 128u : 256u;  // two accumulator buffers
@@ -335,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(smem_u32(&s.full[i]), 1);
-      mbar_init(smem_u32(&s.empty[i]), 1 + 4);  // the MMAs' commit + the 4 epilogue warps
+      mbar_init(smem_u32(&s.empty[i]), 4);  // the 4 epilogue warps
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&s.tfull[i]), 1);
@@ -904,13 +925,15 @@ int launch_indexer_logits(const uint8_t* q, int64_t B, int64_t next_n, int64_t q
   if (items > INT32_MAX) return set_error(FP8MLA_ERR_INVALID_ARGUMENT, "too many indexer work items");
   a.items = (int)items;
   if (a.items == 0) return FP8MLA_OK;
-  const size_t smem = sizeof(idx::Smem) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(idx::indexer_logits_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return check_cuda(e, "indexer logits smem attribute");
   const dim3 grid((unsigned)std::min<int64_t>(items, 2 * (int64_t)sms));
-  return check_cuda(launch_pdl(idx::indexer_logits_kernel, grid, dim3(idx::kThreads), smem, st, a, tm),
-                    "indexer_logits_kernel launch");
+  auto launch = [&](auto kern, size_t smem) -> int {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return check_cuda(e, "indexer logits smem attribute");
+    return check_cuda(launch_pdl(kern, grid, dim3(idx::kThreads), smem, st, a, tm),
+                      "indexer_logits_kernel launch");
+  };
+  if (next_n == 1) return launch(idx::indexer_logits_kernel<1>, sizeof(idx::Smem<1>) + 1024);
+  return launch(idx::indexer_logits_kernel<2>, sizeof(idx::Smem<2>) + 1024);
 }
 
 int launch_indexer_topk(const float* logits, int64_t rows, int64_t logits_stride, int64_t next_n,
