@@ -1,7 +1,7 @@
 """GPU parity of the sm_100a decode against the oracle and the reference's golden vectors.
 
 Mirrors the reference's decode tests (tests/test_sparse_decode.py:44-194) and
-harness sections (verify/run_all.py:78-185), with the north-star tolerance:
+harness sections (verify/run_all.py:78-185), with the decode's stated tolerance:
 max-abs <= 2e-2 and cosine >= 0.9999 against the fp32 golden path.
 """
 
@@ -75,7 +75,8 @@ def test_empty_row_is_zero_with_minus_inf_lse(cuda_device):
 
 
 def test_leading_fully_masked_splits_do_not_poison(cuda_device):
-    """Fully masked leading chunks AND whole leading splits (north-star item 4)."""
+    """Fully masked leading chunks AND whole leading splits: no NaN, the rest
+    of the row unchanged."""
     w = synthetic.make_host("c1", seed=3)
     pool = U.device_pool(w.kv_src_bits)
     slots = w.slots.copy()

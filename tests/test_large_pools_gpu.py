@@ -144,7 +144,7 @@ def test_small_head_kernel_offsets_past_2_31_on_c4_pool(c4_pool):
     _check_requests(out, lse, q, w.kv, slots, w.sm_scale, range(3))
 
 
-def test_c4_full_shape_edges_a_b_at_the_north_star_tolerance(c4_pool):
+def test_c4_full_shape_edges_a_b_at_the_golden_path_tolerance(c4_pool):
     """c4 at full size (B=32, H=64, top-k 2048, 4,194,304 slots) with edges
     (a) the leading 512 indices of 8 requests masked and (b) offsets past 2^31
     (a random permutation of the pool's pages: about a fifth of all selected
